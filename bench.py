@@ -1,0 +1,357 @@
+#!/usr/bin/env python
+"""Benchmark of the fused packed-KV dequantize + decode-attention path on B200.
+
+Metric: packed-KV GB/s (K+V codes plus K+V FP16 scales of the selected blocks, per decode)
+and microseconds per layer-decode, for the 128K-token INT4 GQA configuration: 1 layer,
+131072 tokens, 8 KV heads x 128 dims, 32 query heads, block 128, group 32.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W]           # this implementation
+  python bench.py --impl reference [--steps K] [--warmup W]      # reference CPU decode
+
+N > 1 runs one rank per GPU (launched by torch.distributed.run): the context is N x 131072
+tokens split by token-block ranges, each rank decodes its 1024 blocks and the normalised
+(out, lse) pairs are exchanged with one NCCL all-gather and merged exactly on every rank
+(weak scaling; at N = 8 this is the 1M-token configuration).
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from dataclasses import replace
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "kvssd-attention_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "packed-KV GB/s & us/layer-decode (128K INT4 GQA), % HBM peak"
+WORKLOAD = "c2"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--copies", type=int, default=3,
+                    help="input copies rotated between steps so no step reads from L2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="target duration of the CPU-baseline sample")
+    return ap.parse_args()
+
+
+def peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.file.flush()
+        text = Path(self.file.name).read_text()
+        rows = [r for r in csv.reader(io.StringIO(text)) if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_threads() -> int:
+    """Host threads the oracle uses: one worker per logical CPU (see kvssd_oracle.decode)."""
+    return os.cpu_count() or 1
+
+
+def sample_blocks() -> int:
+    """Blocks per CPU sample: 8-block chunks, several per host thread, at most a full layer."""
+    return min(1024, max(64, 8 * cpu_threads()))
+
+
+def cpu_oracle_run(seconds: float, blocks: int | None = None, min_runs: int = 1) -> dict:
+    """Times the oracle (numpy restatement of kvssd's reference backend) on a bounded sample
+    of the benchmark workload with the same shapes and distributions."""
+    from kvssd_b200.workloads import WORKLOADS, make_layer
+    from oracle import kvssd_oracle as orc
+
+    blocks = blocks or sample_blocks()
+    w = replace(WORKLOADS[WORKLOAD], tokens=blocks * WORKLOADS[WORKLOAD].block_tokens)
+    layer = make_layer(w, 0, "cpu")
+    args = [t.numpy() for t in (layer.packed_k, layer.packed_v, layer.scales_k, layer.scales_v,
+                                layer.valid_tokens)]
+    q = layer.query.float().numpy()
+    nbytes = blocks * w.bytes_per_block
+    runs, t0 = 0, time.perf_counter()
+    while runs < min_runs or time.perf_counter() - t0 < seconds:
+        orc.decode(q, *args, w.bits, w.group_size, 1 / math.sqrt(w.head_dim))
+        runs += 1
+    dt = time.perf_counter() - t0
+    return {"value": nbytes * runs / dt / 1e9, "unit": "GB/s", "cores": cpu_threads(),
+            "kind": "port", "seconds": dt, "runs": runs,
+            "sample": f"{blocks} of 1024 blocks ({blocks * w.block_tokens} tokens) of the c2 "
+                      f"workload shape per run, {runs} runs; numpy restatement of "
+                      "src/kvssd/backends/reference.py, 8-block chunks on "
+                      f"{cpu_threads()} host threads merged exactly"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from kvssd_b200.workloads import WORKLOADS, make_layer
+    from oracle import kvssd_oracle as orc
+
+    blocks = sample_blocks()
+    w = replace(WORKLOADS[WORKLOAD], tokens=blocks * WORKLOADS[WORKLOAD].block_tokens)
+    layer = make_layer(w, 0, "cpu")
+    tensors = [t.numpy() for t in (layer.packed_k, layer.packed_v, layer.scales_k,
+                                   layer.scales_v, layer.valid_tokens)]
+    q = layer.query.float().numpy()
+    step = lambda: orc.decode(q, *tensors, w.bits, w.group_size, 1 / math.sqrt(w.head_dim))  # noqa: E731
+    for _ in range(max(args.warmup, 0)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    nbytes = blocks * w.bytes_per_block
+    value = nbytes / dt / 1e9
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{WORKLOAD} shape, {blocks}-block sample per step",
+                   "kv_heads": w.kv_heads, "head_dim": w.head_dim, "query_heads": w.query_heads,
+                   "block_tokens": w.block_tokens, "bits": w.bits, "group_size": w.group_size},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cpu_threads(), "kind": "port",
+                         "sample": f"{blocks} blocks ({blocks * w.block_tokens} tokens) of the c2 "
+                                   "shape per step; numpy restatement of kvssd's reference "
+                                   "backend, 8-block chunks on all host threads merged exactly "
+                                   "(the reference is Python and is not installed on the GPU "
+                                   "host)"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def run_ours(args) -> None:
+    from kvssd_b200 import B200AttentionBackend, PackedBatch, ops
+    from kvssd_b200.workloads import WORKLOADS, make_layer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} needs {args.gpus} ranks (got WORLD_SIZE={world}); "
+                         "launch with torch.distributed.run")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=device,
+                                timeout=datetime.timedelta(seconds=120))
+
+    w = WORKLOADS[WORKLOAD]
+    # Rank r owns token-block range r of an (N x 131072)-token context (distinct data per rank).
+    base = make_layer(w, layer=rank, device=device)
+    q = base.query
+    pools = [base]
+    for _ in range(1, max(args.copies, 1)):
+        pools.append(type(base)(base.query, base.packed_k.clone(), base.packed_v.clone(),
+                                base.scales_k.clone(), base.scales_v.clone(),
+                                base.valid_tokens.clone()))
+    nbytes = w.blocks_per_layer * w.bytes_per_block
+    qh, d = q.shape
+    scale = 1 / math.sqrt(d)
+    send = torch.empty(qh * d + qh, dtype=torch.float32, device=device)
+    out_v, lse_v = send[: qh * d].view(qh, d), send[qh * d :]
+    recv = torch.empty((world, qh * d + qh), dtype=torch.float32, device=device)
+
+    def exchange_and_merge():
+        dist.all_gather_into_tensor(recv, send)
+        outs = recv[:, : qh * d].reshape(world, qh, d).contiguous()
+        lses = recv[:, qh * d :].contiguous()
+        return ops.merge_chunks(outs, lses)
+
+    def step(i: int):
+        p = pools[i % len(pools)]
+        ops.decode(q, p.packed_k, p.packed_v, p.scales_k, p.scales_v, p.valid_tokens, w.bits,
+                   w.group_size, scale, out=out_v, lse=lse_v)
+        if world > 1:
+            exchange_and_merge()
+
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn, steps: int, warmup: int) -> float:
+        for i in range(warmup):
+            fn(i)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        if dist:
+            dist.barrier()
+        ms = e0.elapsed_time(e1) / steps
+        if dist:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    # ---- device-timed whole step (inputs resident in HBM)
+    with ClockSampler(device.index) as clocks:
+        ms = timed(step, args.steps, max(args.warmup, 3))
+    clock_summary = clocks.summary()
+    value = world * nbytes / (ms * 1e-3) / 1e9
+
+    # ---- roofline leg: the streaming split-KV kernel alone, same inputs and rotation
+    def split_only(i: int):
+        p = pools[i % len(pools)]
+        ops.decode_split(q, p.packed_k, p.packed_v, p.scales_k, p.scales_v, p.valid_tokens,
+                         w.bits, w.group_size, scale)
+
+    kernel_ms = timed(split_only, args.steps, 3)
+    peak, peak_kind = peaks()
+    achieved = nbytes / (kernel_ms * 1e-3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "decode_c2_traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch")
+
+    # ---- end to end through the plugin with host buffers (H2D + decode + D2H each step)
+    backend = B200AttentionBackend()
+    host = [t.cpu().pin_memory() for t in (base.packed_k, base.packed_v, base.scales_k,
+                                            base.scales_v, base.valid_tokens, base.query)]
+    dev_bufs = [torch.empty_like(t, device=device) for t in host]
+    out_host = torch.empty((qh, d), dtype=torch.float32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    d2h = out_host.numel() * 4
+
+    def e2e_step(i: int):
+        for src, dst in zip(host, dev_bufs):
+            dst.copy_(src, non_blocking=True)
+        batch = PackedBatch(*dev_bufs[:5], w.bits, w.group_size)
+        out, lse = backend.run(dev_bufs[5], batch, scale)
+        if world > 1:
+            out_v.copy_(out)
+            lse_v.copy_(lse)
+            out, lse = exchange_and_merge()
+        out_host.copy_(out, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    e2e_ms = timed(e2e_step, e2e_steps, 3)
+    e2e_value = world * nbytes / (e2e_ms * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_oracle_run(args.cpu_seconds)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    launches_per_step = 2 + (1 if world > 1 else 0)
+    record = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {
+            "workload": (f"{WORKLOAD}: 1 layer x 131072 tokens per GPU, INT4 group 32 FP16 "
+                         "scales, 8 KV heads x 128, 32 query heads (GQA 4), block 128, AllBlocks"
+                         + (f"; {world} GPUs split one {world * 131072}-token context by "
+                            "token-block ranges, NCCL all-gather + exact merge" if world > 1 else "")),
+            "us_per_layer_decode": ms * 1e3,
+            "packed_kv_bytes_per_gpu": nbytes,
+            "hbm_peak_gbs": peak,
+            "hbm_frac": value / world / peak,
+            "kv_bits": w.bits,
+            "l2": f"inputs rotated over {len(pools)} copies ({len(pools) * nbytes / 1e6:.0f} MB > 126 MB L2)",
+            "parallelism": f"token-range split x{world}" if world > 1 else "single GPU",
+        },
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel": "tc_decode_kernel<4,128,32> (split-KV stream)",
+                     "kernel_us": kernel_ms * 1e3, "peak_kind": f"{peak_kind} (burst copy)"},
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "path": "B200AttentionBackend.run (C ABI) from pinned host buffers"},
+        "gpu_launches": args.steps * launches_per_step,
+        "clocks": clock_summary,
+    }
+    if cpu is not None:
+        record["cpu_baseline"] = cpu
+    print(json.dumps(record))
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,150 @@
+/*
+ * kvssd_b200.h -- C ABI of the B200 fused dequantize + decode-attention library
+ * (libkvssd_b200.so). Plain pointers and sizes only; every pointer argument except the
+ * stream is a CUDA device pointer on the current device unless stated otherwise.
+ *
+ * Data layout (identical to kvssd's PackedBatch, src/kvssd/backends/base.py:19-27, and to the
+ * record payload of src/kvssd/format.py:104-131):
+ *   packed_k, packed_v : uint8  [n_pool_blocks, block_tokens, kv_heads, head_dim*bits/8]
+ *                        codes packed low-bits-first (src/kvssd/quant.py:28-37)
+ *   scales_k, scales_v : fp16   [n_pool_blocks, block_tokens, kv_heads, head_dim/group_size]
+ *   valid_tokens       : int32  [n_pool_blocks], rows of each block that enter the softmax
+ *   block_table        : int32  [n_sel_blocks], pool index of each selected block, in order;
+ *                        NULL selects blocks 0..n_sel_blocks-1 (the stacked-PackedBatch case)
+ *   query              : [query_heads, head_dim] of type query_dtype (KVSSD_B200_Q_*)
+ *   out, lse           : fp32 [query_heads, head_dim] normalised output, fp32 [query_heads]
+ *                        natural-log normaliser (kvssd's backend contract, base.py:76-81)
+ *
+ * Every entry point returns KVSSD_B200_OK (0) or a status below; none aborts or exits.
+ * Kernels are enqueued on `stream`; the caller keeps all buffers alive until it completes.
+ */
+#ifndef KVSSD_B200_H_
+#define KVSSD_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KVSSD_B200_API __attribute__((visibility("default")))
+#else
+#define KVSSD_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* kvssd_b200_stream_t; /* == cudaStream_t; NULL = legacy stream */
+
+enum kvssd_b200_status {
+  KVSSD_B200_OK = 0,
+  KVSSD_B200_ERR_INVALID_ARGUMENT = 1, /* shape/dtype/pointer contract violated */
+  KVSSD_B200_ERR_UNSUPPORTED = 2,      /* valid kvssd input outside this library's range */
+  KVSSD_B200_ERR_WORKSPACE = 3,        /* workspace missing or smaller than required */
+  KVSSD_B200_ERR_CUDA = 4,             /* a CUDA runtime call or launch failed */
+  KVSSD_B200_ERR_DEVICE_STATUS = 5     /* kernels flagged bad block-table/valid entries */
+};
+
+enum kvssd_b200_query_dtype {
+  KVSSD_B200_Q_F32 = 0,
+  KVSSD_B200_Q_F16 = 1,
+  KVSSD_B200_Q_BF16 = 2,
+  KVSSD_B200_Q_F64 = 3
+};
+
+/* Decode kernel selection, reported by kvssd_b200_decode_path and settable for A/B runs. */
+enum kvssd_b200_path {
+  KVSSD_B200_PATH_AUTO = 0,
+  KVSSD_B200_PATH_TENSOR_CORE = 1, /* mma.sync split-KV kernel (head_dim 64/128/256, group>=16) */
+  KVSSD_B200_PATH_GENERIC = 2      /* CUDA-core split-KV kernel (any head_dim <= 256) */
+};
+
+/* Library ABI version (incremented on any signature change). No reference counterpart. */
+KVSSD_B200_API int kvssd_b200_version(void);
+
+/* Static description of a status code. No reference counterpart. */
+KVSSD_B200_API const char* kvssd_b200_status_string(int status);
+
+/* Detail of the last error raised on the calling thread (empty if none). */
+KVSSD_B200_API const char* kvssd_b200_last_error(void);
+
+/* Bytes of device workspace kvssd_b200_decode needs for this geometry on the current device.
+ * Replaces the per-call torch allocations of the reference op (csrc/fused_decode.cu:125-127). */
+KVSSD_B200_API int kvssd_b200_decode_workspace_size(int n_sel_blocks, int block_tokens, int query_heads,
+                                     int kv_heads, int head_dim, int bits, int group_size,
+                                     size_t* bytes);
+
+/* Fused dequantize + single-token GQA decode attention over the selected packed blocks.
+ * Replaces kvssd._C.fused_decode (csrc/bindings.cpp:16-41 -> csrc/fused_decode.cu:92-142),
+ * bound from CudaExtensionBackend.run (src/kvssd/backends/cuda.py:31-48). Same preconditions
+ * (bindings.cpp:26-38, fused_decode.cu:117-121) plus the block table. Invalid block-table or
+ * valid_tokens entries are never dereferenced: they are skipped/clamped and recorded in the
+ * workspace status word (see kvssd_b200_read_status). Outputs: out, lse as in the header.
+ * The workspace (>= kvssd_b200_decode_workspace_size bytes, 16-byte aligned) starts with that
+ * sticky status word: zero its first 256 bytes once after allocating it. Calls sharing one
+ * workspace must be ordered on the GPU (same stream or explicit events). */
+KVSSD_B200_API int kvssd_b200_decode(const void* query, int query_dtype, const uint8_t* packed_k,
+                      const uint8_t* packed_v, const uint16_t* scales_k,
+                      const uint16_t* scales_v, const int32_t* valid_tokens,
+                      const int32_t* block_table, int n_pool_blocks, int n_sel_blocks,
+                      int block_tokens, int query_heads, int kv_heads, int head_dim, int bits,
+                      int group_size, float sm_scale, float* out, float* lse, void* workspace,
+                      size_t workspace_bytes, kvssd_b200_stream_t stream);
+
+/* The two stages of kvssd_b200_decode, for callers that consume or exchange the split-KV
+ * state themselves (e.g. timing the streaming kernel alone). decode_split takes the decode
+ * arguments minus out/lse, runs the streaming kernel only and returns in *n_parts the number
+ * of (m, l, acc) parts it wrote to the workspace; decode_combine folds them into out/lse.
+ * No reference counterpart (the reference op is a single kernel, csrc/fused_decode.cu:92). */
+KVSSD_B200_API int kvssd_b200_decode_split(const void* query, int query_dtype, const uint8_t* packed_k,
+                            const uint8_t* packed_v, const uint16_t* scales_k,
+                            const uint16_t* scales_v, const int32_t* valid_tokens,
+                            const int32_t* block_table, int n_pool_blocks, int n_sel_blocks,
+                            int block_tokens, int query_heads, int kv_heads, int head_dim,
+                            int bits, int group_size, float sm_scale, void* workspace,
+                            size_t workspace_bytes, int* n_parts, kvssd_b200_stream_t stream);
+KVSSD_B200_API int kvssd_b200_decode_combine(const void* workspace, int n_parts, int query_heads,
+                              int head_dim, float* out, float* lse, kvssd_b200_stream_t stream);
+
+/* Which decode kernel kvssd_b200_decode would run for this geometry (KVSSD_B200_PATH_*).
+ * No reference counterpart (the reference has one kernel). */
+KVSSD_B200_API int kvssd_b200_decode_path(int head_dim, int bits, int group_size, int* path);
+
+/* Process-wide override of the decode kernel choice (KVSSD_B200_PATH_*), for A/B
+ * measurements and tests; AUTO restores the default. No reference counterpart. */
+KVSSD_B200_API int kvssd_b200_set_path_override(int path);
+
+/* Reads (synchronising `stream`) and optionally clears the device status word of a decode
+ * workspace; *device_status receives the OR of flagged conditions (1 = block-table entry out
+ * of range, 2 = valid_tokens entry out of [0, block_tokens]). Returns
+ * KVSSD_B200_ERR_DEVICE_STATUS when it is nonzero. No reference counterpart. */
+KVSSD_B200_API int kvssd_b200_read_status(void* workspace, int clear, unsigned* device_status,
+                           kvssd_b200_stream_t stream);
+
+/* Exact N-way merge of normalised chunks: outs fp32 [n_chunks, query_heads, head_dim],
+ * lses fp32 [n_chunks, query_heads] -> out, lse. Generalises merge_attention_chunks
+ * (src/kvssd/attention.py:91-102) as used by the streamed pipeline
+ * (src/kvssd/pipeline.py:147-153); chunks with lse = -inf contribute nothing. */
+KVSSD_B200_API int kvssd_b200_merge_chunks(const float* outs, const float* lses, int n_chunks, int query_heads,
+                            int head_dim, float* out, float* lse, kvssd_b200_stream_t stream);
+
+/* merge_attention_chunks (src/kvssd/attention.py:91-102), term for term, for two chunks. */
+KVSSD_B200_API int kvssd_b200_merge_pair(const float* left_out, const float* left_lse, const float* right_out,
+                          const float* right_lse, int query_heads, int head_dim, float* out,
+                          float* lse, kvssd_b200_stream_t stream);
+
+/* Materialises unpacked codes and FP16 dequantized values with the decode kernels' register
+ * unpackers, for bit-exact comparison with unpack_codes / dequantize_tensor(q, float16)
+ * (src/kvssd/quant.py:40-46, 68-73). packed uint8 [rows, head_dim*bits/8], scales fp16
+ * [rows, head_dim/group_size] -> values fp16 [rows, head_dim], codes uint8 [rows, head_dim].
+ * mode 0 decodes word-wise (K operand path), mode 1 pairs rows 2r, 2r+1 (V operand path;
+ * rows must be even). */
+KVSSD_B200_API int kvssd_b200_dequantize(const uint8_t* packed, const uint16_t* scales, long long rows,
+                          int head_dim, int bits, int group_size, int mode, uint16_t* values,
+                          uint8_t* codes, kvssd_b200_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVSSD_B200_H_ */

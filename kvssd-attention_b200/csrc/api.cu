@@ -1,0 +1,427 @@
+// C ABI of libkvssd_b200: argument validation, launch planning and kernel dispatch.
+//
+// Validation mirrors the reference's checks so a caller sees the same refusals:
+// PackedBatch.validate (src/kvssd/backends/base.py:29-55), the op bindings
+// (csrc/bindings.cpp:26-38) and the kernel launcher (csrc/fused_decode.cu:117-121).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/kvssd_b200.h"
+#include "common.cuh"
+#include "decode.cuh"
+
+namespace kvb {
+
+using DecodeKernel = void (*)(const DecodeArgs);
+DecodeKernel tc_decode_kernel_for(int bits, int d, int group);
+DecodeKernel simt_decode_kernel_for(int d);
+using DequantKernel = void (*)(const uint8_t*, const __half*, long long, int, int, __half*,
+                               uint8_t*);
+DequantKernel dequant_kernel_for(int bits, int mode);
+
+__global__ void combine_parts_kernel(const float*, const float*, int, int, int, float*, float*);
+__global__ void merge_chunks_kernel(const float*, const float*, int, int, int, float*, float*);
+__global__ void merge_pair_kernel(const float*, const float*, const float*, const float*, int,
+                                  int, float*, float*);
+constexpr int kCombineThreads = 512;  // 32 * kCombineWarps in combine.cu
+
+namespace {
+
+thread_local std::string g_last_error;
+int g_path_override = KVSSD_B200_PATH_AUTO;
+
+int fail(int status, const std::string& msg) {
+  g_last_error = msg;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(KVSSD_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+constexpr size_t kHeaderBytes = 256;  // workspace header: device status word + padding
+constexpr int kMaxParts = 8192;       // bound on split-KV parts (combine shared memory)
+
+struct DeviceInfo {
+  int sms = 0;
+  int max_smem_optin = 0;
+};
+
+DeviceInfo device_info(int dev) {
+  static std::mutex mu;
+  static std::vector<DeviceInfo> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= static_cast<int>(cache.size())) cache.resize(dev + 1);
+  if (cache[dev].sms == 0) {
+    cudaDeviceGetAttribute(&cache[dev].sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&cache[dev].max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin,
+                           dev);
+    if (cache[dev].sms <= 0) cache[dev].sms = 148;
+  }
+  return cache[dev];
+}
+
+int occupancy(DecodeKernel k, int threads) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<void*, int>, int>> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  for (auto& e : cache)
+    if (e.first.first == reinterpret_cast<void*>(k) && e.first.second == threads) return e.second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, threads, 0) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    n = 1;
+  }
+  cache.push_back({{reinterpret_cast<void*>(k), threads}, n});
+  return n;
+}
+
+struct Geometry {
+  int n_sel, bt, qh, kvh, d, bits, group;
+};
+
+// Geometry checks common to all entry points (bits, packing, GQA divisibility).
+int check_geometry(const Geometry& g) {
+  if (g.bits != 2 && g.bits != 4) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "bits must be 2 or 4");
+  if (g.n_sel < 1) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "at least one block is required");
+  if (g.bt < 1 || g.qh < 1 || g.kvh < 1 || g.d < 1 || g.group < 1)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "all dimensions must be positive");
+  if (g.d % g.group) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "group_size must divide head_dim");
+  if ((g.d * g.bits) % 8)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "packed dimension does not match query head dimension");
+  if (g.group % (8 / g.bits))
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "group_size must be positive and pack-aligned");
+  if (g.qh % g.kvh) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "query heads must be divisible by KV heads");
+  if (g.d > 256) return fail(KVSSD_B200_ERR_UNSUPPORTED, "head_dim > 256 is not supported");
+  return KVSSD_B200_OK;
+}
+
+struct Plan {
+  int path = 0;
+  DecodeKernel kernel = nullptr;
+  int gqa = 0, n_qsub = 0, n_vheads = 0, heads_per_cta = 0, wph = 0, n_head_groups = 0;
+  int threads = 0, n_splits = 0, n_parts = 0, tiles_per_block = 0;
+  long long total_tiles = 0;
+  size_t ws_bytes = 0;
+};
+
+int choose_path(int d, int bits, int group) {
+  const bool tc_ok = tc_decode_kernel_for(bits, d, group) != nullptr;
+  if (g_path_override == KVSSD_B200_PATH_GENERIC) return KVSSD_B200_PATH_GENERIC;
+  if (g_path_override == KVSSD_B200_PATH_TENSOR_CORE)
+    return tc_ok ? KVSSD_B200_PATH_TENSOR_CORE : -1;
+  return tc_ok ? KVSSD_B200_PATH_TENSOR_CORE : KVSSD_B200_PATH_GENERIC;
+}
+
+int make_plan(const Geometry& g, bool aligned, Plan& p) {
+  int st = check_geometry(g);
+  if (st) return st;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  const DeviceInfo info = device_info(dev);
+  p.path = choose_path(g.d, g.bits, g.group);
+  if (p.path < 0)
+    return fail(KVSSD_B200_ERR_UNSUPPORTED, "tensor-core path forced for an unsupported shape");
+  if (p.path == KVSSD_B200_PATH_TENSOR_CORE && !aligned) {
+    if (g_path_override == KVSSD_B200_PATH_TENSOR_CORE)
+      return fail(KVSSD_B200_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned packed KV");
+    p.path = KVSSD_B200_PATH_GENERIC;
+  }
+  p.gqa = g.qh / g.kvh;
+  p.n_qsub = (p.gqa + 7) / 8;
+  p.n_vheads = g.kvh * p.n_qsub;
+  if (p.path == KVSSD_B200_PATH_TENSOR_CORE) {
+    p.kernel = tc_decode_kernel_for(g.bits, g.d, g.group);
+    p.heads_per_cta = std::min(p.n_vheads, 8);
+    p.wph = 8 / p.heads_per_cta;
+  } else {
+    p.kernel = simt_decode_kernel_for(g.d);
+    p.heads_per_cta = 1;
+    p.wph = 4;
+  }
+  p.threads = 32 * p.heads_per_cta * p.wph;
+  p.n_head_groups = (p.n_vheads + p.heads_per_cta - 1) / p.heads_per_cta;
+  p.tiles_per_block = (g.bt + 15) / 16;
+  p.total_tiles = static_cast<long long>(g.n_sel) * p.tiles_per_block;
+  const long long resident =
+      static_cast<long long>(info.sms) * occupancy(p.kernel, p.threads) / p.n_head_groups;
+  const long long by_work = (p.total_tiles + 2 * p.wph - 1) / (2 * p.wph);
+  long long splits = std::max(1LL, std::min(resident, by_work));
+  splits = std::min<long long>(splits, kMaxParts / p.wph);
+  p.n_splits = static_cast<int>(splits);
+  p.n_parts = p.n_splits * p.wph;
+  const size_t part_floats = static_cast<size_t>(p.n_parts) * g.qh * (g.d + 2);
+  p.ws_bytes = kHeaderBytes + part_floats * sizeof(float);
+  return KVSSD_B200_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+cudaError_t launch_combine(const float* part_acc, const float* part_ml, int n_parts, int qh, int d,
+                           float* out, float* lse, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(qh, (d + 31) / 32, 1);
+  cfg.blockDim = dim3(kCombineThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(n_parts) * sizeof(float);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, combine_parts_kernel, part_acc, part_ml, n_parts, qh, d, out,
+                            lse);
+}
+
+}  // namespace
+}  // namespace kvb
+
+using namespace kvb;
+
+extern "C" {
+
+int kvssd_b200_version(void) { return 1; }
+
+const char* kvssd_b200_status_string(int status) {
+  switch (status) {
+    case KVSSD_B200_OK: return "ok";
+    case KVSSD_B200_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case KVSSD_B200_ERR_UNSUPPORTED: return "unsupported";
+    case KVSSD_B200_ERR_WORKSPACE: return "workspace too small";
+    case KVSSD_B200_ERR_CUDA: return "CUDA error";
+    case KVSSD_B200_ERR_DEVICE_STATUS: return "device flagged invalid block-table or valid_tokens entries";
+    default: return "unknown status";
+  }
+}
+
+const char* kvssd_b200_last_error(void) { return g_last_error.c_str(); }
+
+int kvssd_b200_decode_workspace_size(int n_sel_blocks, int block_tokens, int query_heads,
+                                     int kv_heads, int head_dim, int bits, int group_size,
+                                     size_t* bytes) {
+  if (!bytes) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "bytes must not be NULL");
+  Plan p;
+  const Geometry g{n_sel_blocks, block_tokens, query_heads, kv_heads, head_dim, bits, group_size};
+  const int st = make_plan(g, true, p);
+  if (st) return st;
+  *bytes = p.ws_bytes;
+  return KVSSD_B200_OK;
+}
+
+int kvssd_b200_decode_path(int head_dim, int bits, int group_size, int* path) {
+  if (!path) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "path must not be NULL");
+  const int p = choose_path(head_dim, bits, group_size);
+  if (p < 0) return fail(KVSSD_B200_ERR_UNSUPPORTED, "tensor-core path forced for an unsupported shape");
+  *path = p;
+  return KVSSD_B200_OK;
+}
+
+int kvssd_b200_set_path_override(int path) {
+  if (path < KVSSD_B200_PATH_AUTO || path > KVSSD_B200_PATH_GENERIC)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "unknown path");
+  g_path_override = path;
+  return KVSSD_B200_OK;
+}
+
+}  // extern "C"
+
+namespace kvb {
+namespace {
+
+// Validates a decode call and fills the kernel arguments and launch plan.
+int prepare_decode(const void* query, int query_dtype, const uint8_t* packed_k,
+                   const uint8_t* packed_v, const uint16_t* scales_k, const uint16_t* scales_v,
+                   const int32_t* valid_tokens, const int32_t* block_table, int n_pool_blocks,
+                   int n_sel_blocks, int block_tokens, int query_heads, int kv_heads,
+                   int head_dim, int bits, int group_size, float sm_scale, void* workspace,
+                   size_t workspace_bytes, DecodeArgs& a, Plan& p) {
+  if (!query || !packed_k || !packed_v || !scales_k || !scales_v || !valid_tokens)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "tensor pointers must not be NULL");
+  if (query_dtype < KVSSD_B200_Q_F32 || query_dtype > KVSSD_B200_Q_F64)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "unknown query dtype");
+  if (n_pool_blocks < 1) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "block pool is empty");
+  if (!block_table && n_sel_blocks > n_pool_blocks)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "more selected blocks than pool blocks");
+  if (!std::isfinite(sm_scale)) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "sm_scale must be finite");
+  if ((reinterpret_cast<uintptr_t>(scales_k) | reinterpret_cast<uintptr_t>(scales_v)) & 1u)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "scales must be 2-byte aligned");
+  const Geometry g{n_sel_blocks, block_tokens, query_heads, kv_heads, head_dim, bits, group_size};
+  int st = make_plan(g, aligned16(packed_k) && aligned16(packed_v), p);
+  if (st) return st;
+  if (!workspace || workspace_bytes < p.ws_bytes)
+    return fail(KVSSD_B200_ERR_WORKSPACE, "workspace needs " + std::to_string(p.ws_bytes) + " bytes");
+  if (reinterpret_cast<uintptr_t>(workspace) & 15u)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+  a.q = query;
+  a.q_dtype = query_dtype;
+  a.kp = packed_k;
+  a.vp = packed_v;
+  a.ks = reinterpret_cast<const __half*>(scales_k);
+  a.vs = reinterpret_cast<const __half*>(scales_v);
+  a.valid = valid_tokens;
+  a.table = block_table;
+  a.n_pool = n_pool_blocks;
+  a.n_sel = n_sel_blocks;
+  a.bt = block_tokens;
+  a.qh = query_heads;
+  a.kvh = kv_heads;
+  a.d = head_dim;
+  a.bits = bits;
+  a.group = group_size;
+  a.gqa = p.gqa;
+  a.n_qsub = p.n_qsub;
+  a.n_vheads = p.n_vheads;
+  a.heads_per_cta = p.heads_per_cta;
+  a.wph = p.wph;
+  a.tiles_per_block = p.tiles_per_block;
+  a.total_tiles = p.total_tiles;
+  a.n_splits = p.n_splits;
+  a.score_scale = sm_scale * 1.4426950408889634f;  // log2(e): scores kept in log2 units
+  char* ws = static_cast<char*>(workspace);
+  a.status = reinterpret_cast<unsigned*>(ws);
+  a.part_ml = reinterpret_cast<float*>(ws + kHeaderBytes);
+  a.part_acc = a.part_ml + static_cast<size_t>(p.n_parts) * query_heads * 2;
+  return KVSSD_B200_OK;
+}
+
+int launch_split(const DecodeArgs& a, const Plan& p, cudaStream_t s) {
+  p.kernel<<<dim3(p.n_splits, p.n_head_groups, 1), dim3(p.threads, 1, 1), 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "decode launch");
+}
+
+}  // namespace
+}  // namespace kvb
+
+extern "C" {
+
+int kvssd_b200_decode(const void* query, int query_dtype, const uint8_t* packed_k,
+                      const uint8_t* packed_v, const uint16_t* scales_k,
+                      const uint16_t* scales_v, const int32_t* valid_tokens,
+                      const int32_t* block_table, int n_pool_blocks, int n_sel_blocks,
+                      int block_tokens, int query_heads, int kv_heads, int head_dim, int bits,
+                      int group_size, float sm_scale, float* out, float* lse, void* workspace,
+                      size_t workspace_bytes, kvssd_b200_stream_t stream) {
+  if (!out || !lse) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "tensor pointers must not be NULL");
+  DecodeArgs a;
+  Plan p;
+  int st = prepare_decode(query, query_dtype, packed_k, packed_v, scales_k, scales_v, valid_tokens,
+                          block_table, n_pool_blocks, n_sel_blocks, block_tokens, query_heads,
+                          kv_heads, head_dim, bits, group_size, sm_scale, workspace,
+                          workspace_bytes, a, p);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  st = launch_split(a, p, s);
+  if (st) return st;
+  cudaError_t e = launch_combine(a.part_acc, a.part_ml, p.n_parts, query_heads, head_dim, out, lse, s);
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "combine launch");
+}
+
+int kvssd_b200_decode_split(const void* query, int query_dtype, const uint8_t* packed_k,
+                            const uint8_t* packed_v, const uint16_t* scales_k,
+                            const uint16_t* scales_v, const int32_t* valid_tokens,
+                            const int32_t* block_table, int n_pool_blocks, int n_sel_blocks,
+                            int block_tokens, int query_heads, int kv_heads, int head_dim,
+                            int bits, int group_size, float sm_scale, void* workspace,
+                            size_t workspace_bytes, int* n_parts, kvssd_b200_stream_t stream) {
+  if (!n_parts) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "n_parts must not be NULL");
+  DecodeArgs a;
+  Plan p;
+  int st = prepare_decode(query, query_dtype, packed_k, packed_v, scales_k, scales_v, valid_tokens,
+                          block_table, n_pool_blocks, n_sel_blocks, block_tokens, query_heads,
+                          kv_heads, head_dim, bits, group_size, sm_scale, workspace,
+                          workspace_bytes, a, p);
+  if (st) return st;
+  *n_parts = p.n_parts;
+  return launch_split(a, p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int kvssd_b200_decode_combine(const void* workspace, int n_parts, int query_heads, int head_dim,
+                              float* out, float* lse, kvssd_b200_stream_t stream) {
+  if (!workspace || !out || !lse) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "NULL pointer");
+  if (n_parts < 1 || n_parts > kMaxParts || query_heads < 1 || head_dim < 1 || head_dim > 256)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "bad part geometry");
+  const float* ml = reinterpret_cast<const float*>(static_cast<const char*>(workspace) + kHeaderBytes);
+  const float* acc = ml + static_cast<size_t>(n_parts) * query_heads * 2;
+  cudaError_t e = launch_combine(acc, ml, n_parts, query_heads, head_dim, out, lse,
+                                 reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "combine launch");
+}
+
+int kvssd_b200_read_status(void* workspace, int clear, unsigned* device_status,
+                           kvssd_b200_stream_t stream) {
+  if (!workspace || !device_status) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "NULL pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  unsigned host = 0;
+  cudaError_t e = cudaMemcpyAsync(&host, workspace, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "status read");
+  if (clear && host) {
+    e = cudaMemsetAsync(workspace, 0, sizeof(unsigned), s);
+    if (e != cudaSuccess) return cuda_fail(e, "status clear");
+  }
+  *device_status = host;
+  if (host) return fail(KVSSD_B200_ERR_DEVICE_STATUS, "device status " + std::to_string(host));
+  return KVSSD_B200_OK;
+}
+
+int kvssd_b200_merge_chunks(const float* outs, const float* lses, int n_chunks, int query_heads,
+                            int head_dim, float* out, float* lse, kvssd_b200_stream_t stream) {
+  if (!outs || !lses || !out || !lse) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "NULL pointer");
+  if (n_chunks < 1 || query_heads < 1 || head_dim < 1)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "at least one chunk is required");
+  if (n_chunks > kMaxParts) return fail(KVSSD_B200_ERR_UNSUPPORTED, "too many chunks");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  merge_chunks_kernel<<<dim3(query_heads, (head_dim + 127) / 128, 1), 128,
+                        static_cast<size_t>(n_chunks) * sizeof(float), s>>>(
+      outs, lses, n_chunks, query_heads, head_dim, out, lse);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "merge launch");
+}
+
+int kvssd_b200_merge_pair(const float* left_out, const float* left_lse, const float* right_out,
+                          const float* right_lse, int query_heads, int head_dim, float* out,
+                          float* lse, kvssd_b200_stream_t stream) {
+  if (!left_out || !left_lse || !right_out || !right_lse || !out || !lse)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "NULL pointer");
+  if (query_heads < 1 || head_dim < 1) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "empty chunk");
+  const long long n = static_cast<long long>(query_heads) * head_dim;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  merge_pair_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
+      left_out, left_lse, right_out, right_lse, query_heads, head_dim, out, lse);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "merge launch");
+}
+
+int kvssd_b200_dequantize(const uint8_t* packed, const uint16_t* scales, long long rows,
+                          int head_dim, int bits, int group_size, int mode, uint16_t* values,
+                          uint8_t* codes, kvssd_b200_stream_t stream) {
+  if (!packed || !scales || !values || !codes) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "NULL pointer");
+  if (bits != 2 && bits != 4) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "bits must be 2 or 4");
+  if (rows < 1 || head_dim < 1 || group_size < 1 || head_dim % group_size)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "group_size must divide head_dim");
+  if ((head_dim * bits) % 32)
+    return fail(KVSSD_B200_ERR_UNSUPPORTED, "rows must be whole 32-bit words of codes");
+  if (group_size % (16 / bits))
+    return fail(KVSSD_B200_ERR_UNSUPPORTED, "group_size must cover whole 16-bit lanes");
+  if (mode != 0 && mode != 1) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "mode must be 0 or 1");
+  if (mode == 1 && (rows % 2)) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "mode 1 needs an even row count");
+  if (reinterpret_cast<uintptr_t>(packed) & 3u) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "packed must be 4-byte aligned");
+  const long long items = mode == 0 ? rows * (head_dim * bits / 32) : (rows / 2) * (head_dim * bits / 16);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  dequant_kernel_for(bits, mode)<<<static_cast<unsigned>((items + 255) / 256), 256, 0, s>>>(
+      packed, reinterpret_cast<const __half*>(scales), rows, head_dim, group_size,
+      reinterpret_cast<__half*>(values), codes);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "dequantize launch");
+}
+
+}  // extern "C"

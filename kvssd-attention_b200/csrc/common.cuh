@@ -1,0 +1,195 @@
+// Shared device helpers for the kvssd B200 decode kernels.
+//
+// Bit layout (the contract of kvssd's quantizer, src/kvssd/quant.py:28-46 and 68-73):
+//   * a row of `head_dim` unsigned codes is packed low-bits-first: element i lives in byte
+//     i / (8/bits) at bit offset (i % (8/bits)) * bits;
+//   * a value is (code - 2^(bits-1)) * scale, with one FP16 scale per `group_size` elements.
+//
+// The unpackers below turn packed codes into FP16 without integer conversions: a code n is
+// OR-ed into the mantissa of the FP16 constant 1024 (0x6400), giving the exact value
+// 1024 + n * 2^s, and one HSUB2/HFMA2 with exactly representable constants removes the
+// offset. Every intermediate is an exactly representable small integer, so the centred
+// code (n - midpoint) is exact and the single HMUL2 by the FP16 scale is one
+// round-to-nearest-even step: bit-identical to kvssd's dequantize_tensor(q, torch.float16),
+// which rounds the exact FP32 product (code - mid) * scale to FP16 once.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <string.h>
+
+namespace kvb {
+
+// Query element types accepted by the C ABI (the reference dispatches f32/f64/f16/bf16,
+// csrc/fused_decode.cu:131-140).
+enum QueryDtype : int { kQF32 = 0, kQF16 = 1, kQBF16 = 2, kQF64 = 3 };
+
+// Status bits OR-ed into the workspace header word by device code.
+enum DeviceStatusBits : unsigned {
+  kDevBadBlockIndex = 1u,   // a block-table entry outside [0, n_pool_blocks)
+  kDevBadValidCount = 2u,   // a valid_tokens entry outside [0, block_tokens]
+};
+
+__device__ __forceinline__ float load_query(const void* q, int dtype, long long idx) {
+  switch (dtype) {
+    case kQF16: return __half2float(reinterpret_cast<const __half*>(q)[idx]);
+    case kQBF16: return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(q)[idx]);
+    case kQF64: return static_cast<float>(reinterpret_cast<const double*>(q)[idx]);
+    default: return reinterpret_cast<const float*>(q)[idx];
+  }
+}
+
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t u) {
+  __half2 h;
+  memcpy(&h, &u, 4);
+  return h;
+}
+
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) {
+  uint32_t u;
+  memcpy(&u, &h, 4);
+  return u;
+}
+
+__device__ __forceinline__ __half2 h2_const(uint32_t bits) { return u32_as_h2(bits); }
+
+// (x & MASK) | 0x64006400: places the selected code bits of both 16-bit lanes into the
+// mantissa of FP16 1024.
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t or_magic(uint32_t x) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "n"(MASK), "n"(0x64006400u));
+  return r;
+}
+
+// Centred codes of a 32-bit word viewed as two 16-bit lanes. Lane 0 is bits 0-15, lane 1 is
+// bits 16-31; each lane holds 16/BITS codes in element order. Output pair k is
+// (lane0 code k - mid, lane1 code k - mid) as an exact FP16 pair.
+template <int BITS>
+struct LanePairs;
+
+template <>
+struct LanePairs<4> {
+  static constexpr int kPairs = 4;  // codes per 16-bit lane
+  __device__ __forceinline__ static void centred(uint32_t x, __half2 (&o)[4]) {
+    const uint32_t x8 = x >> 8;
+    // code at bits 0-3 of each lane: 1024 + n, minus 1032 (0x6408)
+    o[0] = __hsub2(u32_as_h2(or_magic<0x000F000Fu>(x)), h2_const(0x64086408u));
+    // code at bits 4-7: 1024 + 16n; times 1/16 (0x2C00) minus 72 (0xD480 = -72)
+    o[1] = __hfma2(u32_as_h2(or_magic<0x00F000F0u>(x)), h2_const(0x2C002C00u),
+                   h2_const(0xD480D480u));
+    o[2] = __hsub2(u32_as_h2(or_magic<0x000F000Fu>(x8)), h2_const(0x64086408u));
+    o[3] = __hfma2(u32_as_h2(or_magic<0x00F000F0u>(x8)), h2_const(0x2C002C00u),
+                   h2_const(0xD480D480u));
+  }
+};
+
+template <>
+struct LanePairs<2> {
+  static constexpr int kPairs = 8;
+  __device__ __forceinline__ static void centred(uint32_t x, __half2 (&o)[8]) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t y = half ? (x >> 8) : x;
+      // bits 0-1: 1024 + n, minus 1026 (0x6402)
+      o[4 * half + 0] = __hsub2(u32_as_h2(or_magic<0x00030003u>(y)), h2_const(0x64026402u));
+      // bits 2-3: 1024 + 4n; * 1/4 (0x3400) - 258 (0xDC08)
+      o[4 * half + 1] = __hfma2(u32_as_h2(or_magic<0x000C000Cu>(y)), h2_const(0x34003400u),
+                                h2_const(0xDC08DC08u));
+      // bits 4-5: 1024 + 16n; * 1/16 (0x2C00) - 66 (0xD420)
+      o[4 * half + 2] = __hfma2(u32_as_h2(or_magic<0x00300030u>(y)), h2_const(0x2C002C00u),
+                                h2_const(0xD420D420u));
+      // bits 6-7: 1024 + 64n; * 1/64 (0x2400) - 18 (0xCC80)
+      o[4 * half + 3] = __hfma2(u32_as_h2(or_magic<0x00C000C0u>(y)), h2_const(0x24002400u),
+                                h2_const(0xCC80CC80u));
+    }
+  }
+};
+
+// Dequantized pairs: centred code times the per-lane FP16 scale, one RN-even rounding.
+template <int BITS>
+__device__ __forceinline__ void dequant_pairs(uint32_t x, __half2 scale,
+                                              __half2 (&o)[LanePairs<BITS>::kPairs]) {
+  LanePairs<BITS>::centred(x, o);
+#pragma unroll
+  for (int k = 0; k < LanePairs<BITS>::kPairs; ++k) o[k] = __hmul2(o[k], scale);
+}
+
+// Combines 16-bit lane `hw` of two 32-bit words (two token rows) into one word whose low
+// lane comes from `a` and high lane from `b`.
+__device__ __forceinline__ uint32_t pair_lanes(uint32_t a, uint32_t b, int hw_in_word) {
+  return __byte_perm(a, b, hw_in_word ? 0x7632u : 0x5410u);
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// D = A * B + D for one m16n8k16 FP16 tile with FP32 accumulation (PTX ISA
+// "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32").
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Transposes an 8x8 b16 matrix held in the mma row-fragment layout.
+__device__ __forceinline__ uint32_t transpose_8x8(uint32_t x) {
+  uint32_t y;
+  asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+template <int N>
+struct VecBytes;  // streaming loads of N contiguous bytes into 32-bit words
+
+template <>
+struct VecBytes<32> {
+  __device__ __forceinline__ static void load(const uint8_t* p, uint32_t* w) {
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]) : "l"(p));
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7]) : "l"(p + 16));
+  }
+};
+template <>
+struct VecBytes<16> {
+  __device__ __forceinline__ static void load(const uint8_t* p, uint32_t* w) {
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]) : "l"(p));
+  }
+};
+template <>
+struct VecBytes<8> {
+  __device__ __forceinline__ static void load(const uint8_t* p, uint32_t* w) {
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+                 : "=r"(w[0]), "=r"(w[1]) : "l"(p));
+  }
+};
+template <>
+struct VecBytes<4> {
+  __device__ __forceinline__ static void load(const uint8_t* p, uint32_t* w) {
+    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(w[0]) : "l"(p));
+  }
+};
+template <>
+struct VecBytes<2> {
+  __device__ __forceinline__ static void load(const uint8_t* p, uint32_t* w) {
+    unsigned short s;
+    asm("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(s) : "l"(p));
+    w[0] = s;
+  }
+};
+
+__device__ __forceinline__ __half load_scale(const __half* p) {
+  unsigned short s;
+  asm("ld.global.nc.u16 %0, [%1];" : "=h"(s) : "l"(p));
+  return __ushort_as_half(s);
+}
+
+}  // namespace kvb

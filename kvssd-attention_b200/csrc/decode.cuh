@@ -1,0 +1,79 @@
+// Launch arguments shared by the split-KV decode kernels and the host dispatcher.
+//
+// Work decomposition (all kernels):
+//   * a "virtual head" is one KV head together with up to 8 of its query heads (GQA ratios
+//     above 8 use several virtual heads per KV head);
+//   * a "tile" is 16 consecutive token rows of one selected block; the selection's tiles are
+//     numbered slot-major (slot = position in the block table, tiles_per_block per slot);
+//   * grid.x = split: CTA x owns tiles [T*x/n_splits, T*(x+1)/n_splits) for every virtual
+//     head of its head group (grid.y), so the CTA's warps read whole token rows (all KV
+//     heads of a token are contiguous in kvssd's record layout, src/kvssd/format.py:165);
+//   * each warp keeps an online-softmax state (m, l, acc) per query head and writes it as one
+//     "part" of the split-KV result; part = split * wph + warp-subindex.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace kvb {
+
+struct DecodeArgs {
+  const void* q;
+  int q_dtype;
+  const uint8_t* kp;   // [n_pool, bt, kvh, d*bits/8]
+  const uint8_t* vp;   // [n_pool, bt, kvh, d*bits/8]
+  const __half* ks;    // [n_pool, bt, kvh, d/group]
+  const __half* vs;    // [n_pool, bt, kvh, d/group]
+  const int32_t* valid;  // [n_pool]
+  const int32_t* table;  // [n_sel] pool indices, or nullptr for the identity
+  int n_pool, n_sel, bt, qh, kvh, d, bits, group;
+  int gqa;            // query heads per KV head
+  int n_qsub;         // virtual heads per KV head
+  int n_vheads;       // kvh * n_qsub
+  int heads_per_cta;  // virtual heads handled by one CTA
+  int wph;            // warps per virtual head in a CTA (they interleave tiles)
+  int tiles_per_block;
+  long long total_tiles;
+  int n_splits;
+  float score_scale;  // sm_scale * log2(e): scores are kept in the log2 domain
+  float* part_acc;    // [n_parts, qh, d] unnormalised sum p*v
+  float* part_ml;     // [n_parts, qh, 2]  (running max in log2 domain, sum of p)
+  unsigned* status;   // device status word (DeviceStatusBits)
+};
+
+// Resolves slot -> (pool block, clamped valid count) with a per-warp register cache of 32
+// consecutive slots, so the dependent block-table/valid loads are paid once per 32 blocks.
+struct BlockInfoCache {
+  int base = -0x40000000;
+  int blk = -1;
+  int valid = 0;
+
+  __device__ __forceinline__ void lookup(const DecodeArgs& a, int slot, int lane, int& out_blk,
+                                         int& out_valid) {
+    if (slot < base || slot - base >= 32) {  // warp-uniform: slot is the same on all lanes
+      base = slot;
+      const int s = slot + lane;
+      blk = -1;
+      valid = 0;
+      if (s < a.n_sel) {
+        int b = a.table ? a.table[s] : s;
+        if (b < 0 || b >= a.n_pool) {
+          atomicOr(a.status, 1u);
+          b = -1;
+        } else {
+          int v = a.valid[b];
+          if (v < 0 || v > a.bt) {
+            atomicOr(a.status, 2u);
+            v = v < 0 ? 0 : a.bt;
+          }
+          valid = v;
+        }
+        blk = b;
+      }
+    }
+    out_blk = __shfl_sync(0xffffffffu, blk, slot - base);
+    out_valid = __shfl_sync(0xffffffffu, valid, slot - base);
+  }
+};
+
+}  // namespace kvb

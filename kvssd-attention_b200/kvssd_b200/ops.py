@@ -1,0 +1,321 @@
+"""Torch-tensor wrappers over the C ABI (include/kvssd_b200.h).
+
+Every function here launches CUDA kernels from libkvssd_b200 on the current CUDA stream of
+the tensors' device; none has a CPU path. Tensors are passed by data pointer, so callers must
+pass contiguous CUDA tensors (the wrappers check and raise otherwise).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import threading
+
+import torch
+
+from . import _native
+
+_QUERY_DTYPES = {
+    torch.float32: _native.Q_F32,
+    torch.float16: _native.Q_F16,
+    torch.bfloat16: _native.Q_BF16,
+    torch.float64: _native.Q_F64,
+}
+
+_WORKSPACE_HEADER = 256
+
+
+class _Workspaces:
+    """Per-(device, stream) decode workspaces, grown on demand and reused across calls.
+
+    Reuse is safe because calls that share a workspace are ordered on one stream; the
+    header's device status word is zeroed once at allocation (it accumulates until read).
+    """
+
+    def __init__(self) -> None:
+        self._lock = threading.Lock()
+        self._buffers: dict[tuple[int, int], torch.Tensor] = {}
+
+    def get(self, device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor:
+        key = (device.index, stream.cuda_stream)
+        with self._lock:
+            buf = self._buffers.get(key)
+            if buf is None or buf.numel() < nbytes:
+                size = max(nbytes, 1 << 20)
+                if buf is not None:
+                    size = max(size, 2 * buf.numel())
+                buf = torch.zeros(size, dtype=torch.uint8, device=device)
+                self._buffers[key] = buf
+            return buf
+
+
+_workspaces = _Workspaces()
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(name: str, t: torch.Tensor, device: torch.device, dtype: torch.dtype) -> None:
+    if t.device != device:
+        raise ValueError(f"{name} must be on {device}, got {t.device}")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _decode_args(query, packed_k, packed_v, scales_k, scales_v, valid_tokens, bits, group_size,
+                 block_table):
+    """Validates decode tensors; returns (query, geometry tuple, n_sel)."""
+    device = query.device
+    if device.type != "cuda":
+        raise RuntimeError(f"kvssd_b200 decode requires a CUDA device, got {device}")
+    if query.ndim != 2:
+        raise ValueError("query must be [query_heads, head_dim]")
+    if query.dtype not in _QUERY_DTYPES:
+        raise ValueError(f"unsupported query dtype {query.dtype}")
+    if not query.is_contiguous():
+        query = query.contiguous()
+    if packed_k.ndim != 4 or packed_k.shape != packed_v.shape:
+        raise ValueError("packed KV must match [blocks,tokens,kv_heads,packed_dim]")
+    if scales_k.ndim != 4 or scales_k.shape != scales_v.shape:
+        raise ValueError("KV scales must match [blocks,tokens,kv_heads,groups]")
+    for name, t, dt in (("packed_k", packed_k, torch.uint8), ("packed_v", packed_v, torch.uint8),
+                        ("scales_k", scales_k, torch.float16), ("scales_v", scales_v, torch.float16),
+                        ("valid_tokens", valid_tokens, torch.int32)):
+        _require_cuda(name, t, device, dt)
+    n_pool, bt, kvh, pd = packed_k.shape
+    qh, d = query.shape
+    if tuple(scales_k.shape[:3]) != (n_pool, bt, kvh) or scales_k.shape[3] * group_size != d:
+        raise ValueError("scale dimension mismatch")
+    if valid_tokens.shape != (n_pool,):
+        raise ValueError("valid_tokens must contain one count per block")
+    if pd * 8 != d * bits:
+        raise ValueError("packed dimension does not match query head dimension")
+    if block_table is not None:
+        _require_cuda("block_table", block_table, device, torch.int32)
+        if block_table.ndim != 1:
+            raise ValueError("block_table must be 1-D")
+        n_sel = block_table.shape[0]
+    else:
+        n_sel = n_pool
+    return query, (n_pool, n_sel, bt, qh, kvh, d, bits, group_size)
+
+
+def _workspace_for(device, geometry) -> tuple[torch.Tensor, torch.cuda.Stream]:
+    n_pool, n_sel, bt, qh, kvh, d, bits, group_size = geometry
+    need = ctypes.c_size_t()
+    _native.check(
+        _native.library().kvssd_b200_decode_workspace_size(n_sel, bt, qh, kvh, d, bits,
+                                                           group_size, ctypes.byref(need)),
+        "kvssd_b200_decode_workspace_size",
+    )
+    stream = torch.cuda.current_stream(device)
+    return _workspaces.get(device, stream, need.value), stream
+
+
+def decode(
+    query: torch.Tensor,
+    packed_k: torch.Tensor,
+    packed_v: torch.Tensor,
+    scales_k: torch.Tensor,
+    scales_v: torch.Tensor,
+    valid_tokens: torch.Tensor,
+    bits: int,
+    group_size: int,
+    sm_scale: float,
+    block_table: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    lse: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Fused dequantize + decode attention; returns (out fp32 [QH, D], lse fp32 [QH]).
+
+    ``packed_*``/``scales_*``/``valid_tokens`` form a block pool; ``block_table`` (int32
+    [n_sel]) selects and orders pool blocks (None = all pool blocks in order).
+    """
+    query, geom = _decode_args(query, packed_k, packed_v, scales_k, scales_v, valid_tokens, bits,
+                               group_size, block_table)
+    device = query.device
+    n_pool, n_sel, bt, qh, kvh, d, _, _ = geom
+    with torch.cuda.device(device):
+        ws, stream = _workspace_for(device, geom)
+        if out is None:
+            out = torch.empty((qh, d), dtype=torch.float32, device=device)
+        if lse is None:
+            lse = torch.empty((qh,), dtype=torch.float32, device=device)
+        _require_cuda("out", out, device, torch.float32)
+        _require_cuda("lse", lse, device, torch.float32)
+        status = _native.library().kvssd_b200_decode(
+            _ptr(query), _QUERY_DTYPES[query.dtype],
+            _ptr(packed_k), _ptr(packed_v), _ptr(scales_k), _ptr(scales_v),
+            _ptr(valid_tokens), _ptr(block_table),
+            n_pool, n_sel, bt, qh, kvh, d, bits, group_size,
+            float(sm_scale), _ptr(out), _ptr(lse),
+            _ptr(ws), ws.numel(), stream.cuda_stream,
+        )
+        _native.check(status, "kvssd_b200_decode")
+    return out, lse
+
+
+def decode_split(query, packed_k, packed_v, scales_k, scales_v, valid_tokens, bits: int,
+                 group_size: int, sm_scale: float, block_table=None) -> tuple[int, torch.Tensor]:
+    """Runs only the streaming split-KV kernel; returns (n_parts, workspace).
+
+    The parts stay in the returned workspace until the next decode on this stream;
+    decode_combine folds them into (out, lse).
+    """
+    query, geom = _decode_args(query, packed_k, packed_v, scales_k, scales_v, valid_tokens, bits,
+                               group_size, block_table)
+    device = query.device
+    n_pool, n_sel, bt, qh, kvh, d, _, _ = geom
+    n_parts = ctypes.c_int()
+    with torch.cuda.device(device):
+        ws, stream = _workspace_for(device, geom)
+        status = _native.library().kvssd_b200_decode_split(
+            _ptr(query), _QUERY_DTYPES[query.dtype],
+            _ptr(packed_k), _ptr(packed_v), _ptr(scales_k), _ptr(scales_v),
+            _ptr(valid_tokens), _ptr(block_table),
+            n_pool, n_sel, bt, qh, kvh, d, bits, group_size, float(sm_scale),
+            _ptr(ws), ws.numel(), ctypes.byref(n_parts), stream.cuda_stream,
+        )
+        _native.check(status, "kvssd_b200_decode_split")
+    return n_parts.value, ws
+
+
+def decode_combine(workspace: torch.Tensor, n_parts: int, query_heads: int, head_dim: int,
+                   out: torch.Tensor | None = None, lse: torch.Tensor | None = None):
+    device = workspace.device
+    if out is None:
+        out = torch.empty((query_heads, head_dim), dtype=torch.float32, device=device)
+    if lse is None:
+        lse = torch.empty((query_heads,), dtype=torch.float32, device=device)
+    with torch.cuda.device(device):
+        _native.check(
+            _native.library().kvssd_b200_decode_combine(
+                _ptr(workspace), n_parts, query_heads, head_dim, _ptr(out), _ptr(lse),
+                _stream_handle(device)),
+            "kvssd_b200_decode_combine",
+        )
+    return out, lse
+
+
+def read_device_status(device: torch.device | str | None = None, clear: bool = True) -> int:
+    """Synchronously reads the sticky device status word of the current stream's workspace.
+
+    Bit 1: a block-table entry was outside the pool; bit 2: a valid_tokens entry was outside
+    [0, block_tokens]. Such entries are skipped/clamped by the kernels, never dereferenced.
+    """
+    device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(device)
+    ws = _workspaces.get(device, stream, _WORKSPACE_HEADER)
+    value = ctypes.c_uint()
+    with torch.cuda.device(device):
+        status = _native.library().kvssd_b200_read_status(
+            _ptr(ws), 1 if clear else 0, ctypes.byref(value), stream.cuda_stream
+        )
+    if status not in (_native.OK, _native.ERR_DEVICE_STATUS):
+        _native.check(status, "kvssd_b200_read_status")
+    return int(value.value)
+
+
+def decode_path(head_dim: int, bits: int, group_size: int) -> int:
+    path = ctypes.c_int()
+    _native.check(
+        _native.library().kvssd_b200_decode_path(head_dim, bits, group_size, ctypes.byref(path)),
+        "kvssd_b200_decode_path",
+    )
+    return path.value
+
+
+def set_path_override(path: int) -> None:
+    _native.check(_native.library().kvssd_b200_set_path_override(path), "set_path_override")
+
+
+def merge_chunks(outs: torch.Tensor, lses: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Exact N-way merge of normalised chunks: outs [N, QH, D] fp32, lses [N, QH] fp32."""
+    device = outs.device
+    if device.type != "cuda":
+        raise RuntimeError(f"merge_chunks requires CUDA tensors, got {device}")
+    if outs.ndim != 3 or lses.shape != outs.shape[:2]:
+        raise ValueError("expected outs [N, QH, D] and lses [N, QH]")
+    _require_cuda("outs", outs, device, torch.float32)
+    _require_cuda("lses", lses, device, torch.float32)
+    n, qh, d = outs.shape
+    out = torch.empty((qh, d), dtype=torch.float32, device=device)
+    lse = torch.empty((qh,), dtype=torch.float32, device=device)
+    with torch.cuda.device(device):
+        _native.check(
+            _native.library().kvssd_b200_merge_chunks(
+                _ptr(outs), _ptr(lses), n, qh, d, _ptr(out), _ptr(lse), _stream_handle(device)
+            ),
+            "kvssd_b200_merge_chunks",
+        )
+    return out, lse
+
+
+def merge_pair(
+    left_output: torch.Tensor, left_lse: torch.Tensor, right_output: torch.Tensor,
+    right_lse: torch.Tensor,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    device = left_output.device
+    if device.type != "cuda":
+        raise RuntimeError(f"merge_attention_chunks requires CUDA tensors, got {device}")
+    if left_output.ndim != 2 or right_output.shape != left_output.shape:
+        raise ValueError("chunk outputs must both be [QH, D]")
+    qh, d = left_output.shape
+    if left_lse.shape != (qh,) or right_lse.shape != (qh,):
+        raise ValueError("chunk LSEs must be [QH]")
+    tensors = [t.contiguous().float() for t in (left_output, left_lse, right_output, right_lse)]
+    for name, t in zip(("left_output", "left_lse", "right_output", "right_lse"), tensors):
+        _require_cuda(name, t, device, torch.float32)
+    out = torch.empty((qh, d), dtype=torch.float32, device=device)
+    lse = torch.empty((qh,), dtype=torch.float32, device=device)
+    with torch.cuda.device(device):
+        _native.check(
+            _native.library().kvssd_b200_merge_pair(
+                *map(_ptr, tensors), qh, d, _ptr(out), _ptr(lse), _stream_handle(device)
+            ),
+            "kvssd_b200_merge_pair",
+        )
+    return out, lse
+
+
+def dequantize_packed(
+    packed: torch.Tensor, scales: torch.Tensor, bits: int, group_size: int, mode: int = 0
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Runs the decode kernels' register unpacker over [rows, packed_dim] codes.
+
+    Returns (codes uint8 [rows, D], values fp16 [rows, D]); used to prove bit-exactness
+    against kvssd's unpack_codes / dequantize_tensor(q, torch.float16).
+    """
+    device = packed.device
+    if device.type != "cuda":
+        raise RuntimeError(f"dequantize_packed requires CUDA tensors, got {device}")
+    pd = packed.shape[-1]
+    d = pd * 8 // bits
+    rows = packed.numel() // pd
+    p2 = packed.reshape(rows, pd).contiguous()
+    s2 = scales.reshape(rows, -1).contiguous()
+    _require_cuda("packed", p2, device, torch.uint8)
+    _require_cuda("scales", s2, device, torch.float16)
+    values = torch.empty((rows, d), dtype=torch.float16, device=device)
+    codes = torch.empty((rows, d), dtype=torch.uint8, device=device)
+    with torch.cuda.device(device):
+        _native.check(
+            _native.library().kvssd_b200_dequantize(
+                _ptr(p2), _ptr(s2), rows, d, bits, group_size, mode, _ptr(values), _ptr(codes),
+                _stream_handle(device),
+            ),
+            "kvssd_b200_dequantize",
+        )
+    shape = (*packed.shape[:-1], d)
+    return codes.reshape(shape), values.reshape(shape)
+
+
+def default_sm_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

@@ -1,0 +1,161 @@
+"""KVCacheStore: append-only fixed-record KV cache file plus manifest.
+
+API-compatible with src/kvssd/store.py:20-113 (create / open / entry / blocks_for_layer /
+read_into / read / close) and byte-compatible on disk. Storage is positioned reads (pread)
+of whole 4 KiB-aligned records; the reference's O_DIRECT and cuFile storage backends are not
+part of this package.
+"""
+
+from __future__ import annotations
+
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+from .format import BlockEntry, CacheSpec, Manifest, PackedKVBlock, decode_record, encode_record
+from .quant import quantize_tensor
+
+DATA_FILE = "blocks.kvssd"
+MANIFEST_FILE = "manifest.json"
+
+
+class _PreadFile:
+    """One lazily opened read-only descriptor shared by reader threads."""
+
+    def __init__(self, path: Path):
+        self.path = path
+        self._fd: int | None = None
+        self._lock = threading.Lock()
+
+    def fd(self) -> int:
+        with self._lock:
+            if self._fd is None:
+                self._fd = os.open(self.path, os.O_RDONLY)
+            return self._fd
+
+    def read_into(self, entry: BlockEntry, destination: torch.Tensor) -> None:
+        if destination.device.type != "cpu":
+            raise ValueError("record reads require a CPU destination tensor")
+        if destination.dtype != torch.uint8 or destination.numel() < entry.length:
+            raise ValueError("destination must be a sufficiently large uint8 tensor")
+        target = memoryview(destination[: entry.length].numpy())
+        got = os.preadv(self.fd(), [target], entry.offset)
+        if got != entry.length:
+            raise EOFError(
+                f"short read for layer={entry.layer}, block={entry.block}: "
+                f"expected {entry.length}, got {got}"
+            )
+
+    def close(self) -> None:
+        with self._lock:
+            if self._fd is not None:
+                os.close(self._fd)
+                self._fd = None
+
+
+class KVCacheStore:
+    """Append-only fixed-record KV cache store designed for large sequential reads."""
+
+    def __init__(self, root: str | Path, manifest: Manifest, storage_backend: str | None = None):
+        if storage_backend not in (None, "auto", "buffered"):
+            raise ValueError(
+                f"storage backend '{storage_backend}' is not provided by kvssd_b200; "
+                "use 'buffered' (positioned reads)"
+            )
+        self.root = Path(root)
+        self.manifest = manifest
+        self.spec = manifest.spec
+        self._entries = {(e.layer, e.block): e for e in manifest.entries}
+        self._layer_blocks: dict[int, list[int]] = {}
+        for e in manifest.entries:
+            self._layer_blocks.setdefault(e.layer, []).append(e.block)
+        for blocks in self._layer_blocks.values():
+            blocks.sort()
+        self._file = _PreadFile(self.root / DATA_FILE)
+
+    @classmethod
+    def create(
+        cls,
+        root: str | Path,
+        keys: torch.Tensor,
+        values: torch.Tensor,
+        spec: CacheSpec,
+        storage_backend: str | None = None,
+    ) -> "KVCacheStore":
+        """Creates a store from [layers, tokens, kv_heads, head_dim] tensors.
+
+        Tokens are cut into blocks of ``block_tokens``; the last block of a layer is
+        zero-padded and records its valid row count (src/kvssd/store.py:27-67).
+        """
+        spec.validate()
+        if keys.shape != values.shape or keys.ndim != 4:
+            raise ValueError("keys and values must share [layers,tokens,kv_heads,head_dim]")
+        if keys.shape[0] != spec.layers or tuple(keys.shape[2:]) != (spec.kv_heads, spec.head_dim):
+            raise ValueError("input tensors do not match CacheSpec")
+        root = Path(root)
+        root.mkdir(parents=True, exist_ok=True)
+        shape = (spec.block_tokens, spec.kv_heads, spec.head_dim)
+        entries: list[BlockEntry] = []
+        with (root / DATA_FILE).open("wb") as out:
+            for layer in range(spec.layers):
+                for block_id, start in enumerate(range(0, keys.shape[1], spec.block_tokens)):
+                    valid = min(spec.block_tokens, keys.shape[1] - start)
+                    k = torch.zeros(shape, dtype=keys.dtype)
+                    v = torch.zeros(shape, dtype=values.dtype)
+                    k[:valid].copy_(keys[layer, start : start + valid].cpu())
+                    v[:valid].copy_(values[layer, start : start + valid].cpu())
+                    block = PackedKVBlock(
+                        layer, block_id, valid,
+                        quantize_tensor(k, spec.bits, spec.group_size),
+                        quantize_tensor(v, spec.bits, spec.group_size),
+                    )
+                    record, crc = encode_record(block, spec)
+                    offset = out.tell()
+                    out.write(record)
+                    entries.append(BlockEntry(layer, block_id, offset, len(record), valid, crc))
+        manifest = Manifest(spec=spec, entries=entries)
+        manifest.save(root / MANIFEST_FILE)
+        return cls(root, manifest, storage_backend)
+
+    @classmethod
+    def open(cls, root: str | Path, storage_backend: str | None = None) -> "KVCacheStore":
+        root = Path(root)
+        manifest = Manifest.load(root / MANIFEST_FILE)
+        manifest.spec.validate()
+        return cls(root, manifest, storage_backend)
+
+    def entry(self, layer: int, block: int) -> BlockEntry:
+        try:
+            return self._entries[(layer, block)]
+        except KeyError as exc:
+            raise KeyError(f"no KV block layer={layer}, block={block}") from exc
+
+    def blocks_for_layer(self, layer: int) -> list[int]:
+        """Sorted block ids of a layer (precomputed; the reference scans all entries)."""
+        return list(self._layer_blocks.get(layer, []))
+
+    def read_into(self, entry: BlockEntry, destination: torch.Tensor) -> None:
+        self._file.read_into(entry, destination)
+
+    def read(self, layer: int, block: int, verify_crc: bool = True) -> PackedKVBlock:
+        entry = self.entry(layer, block)
+        raw = torch.empty(entry.length, dtype=torch.uint8)
+        self.read_into(entry, raw)
+        return decode_record(raw, self.spec, verify_crc)
+
+    def close(self) -> None:
+        self._file.close()
+
+    def __enter__(self) -> "KVCacheStore":
+        return self
+
+    def __exit__(self, *_: object) -> None:
+        self.close()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,107 @@
+"""The C ABI library loads and exports exactly what include/kvssd_b200.h declares.
+
+No kernel is launched here; argument checks that run before any CUDA call are exercised.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+from conftest import ROOT
+
+from kvssd_b200 import _native
+
+HEADER = ROOT / "include" / "kvssd_b200.h"
+
+
+def declared_functions() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"KVSSD_B200_API\s+[\w\s\*]+?\b(kvssd_b200_\w+)\s*\(", text))
+
+
+def test_header_and_binding_agree():
+    assert declared_functions() == set(_native.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.library()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_native.LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert exported == declared_functions(), "library exports only the declared ABI"
+
+
+def test_version_and_status_strings():
+    lib = _native.library()
+    assert lib.kvssd_b200_version() == 1
+    assert _native.status_string(0) == "ok"
+    for s in range(1, 6):
+        assert _native.status_string(s) not in ("ok", "unknown status")
+
+
+def test_decode_rejects_null_pointers_before_touching_cuda():
+    lib = _native.library()
+    args = [None, 0, None, None, None, None, None, None, 1, 1, 8, 4, 2, 32, 4, 16, 0.1, None, None,
+            None, 0, None]
+    assert lib.kvssd_b200_decode(*args) == _native.ERR_INVALID_ARGUMENT
+    assert b"NULL" in lib.kvssd_b200_last_error()
+
+
+def test_workspace_query_rejects_bad_geometry_before_touching_cuda():
+    lib = _native.library()
+    n = ctypes.c_size_t()
+    cases = [
+        ((1, 8, 4, 2, 32, 3, 16), b"bits"),
+        ((0, 8, 4, 2, 32, 4, 16), b"at least one block"),
+        ((1, 8, 4, 2, 32, 4, 12), b"divide"),
+        ((1, 8, 3, 2, 32, 4, 16), b"divisible by KV heads"),
+        ((1, 8, 4, 2, 36, 2, 6), b"pack-aligned"),
+    ]
+    for geom, msg in cases:
+        assert lib.kvssd_b200_decode_workspace_size(*geom, ctypes.byref(n)) == _native.ERR_INVALID_ARGUMENT
+        assert msg in lib.kvssd_b200_last_error()
+    assert lib.kvssd_b200_decode_workspace_size(1, 8, 4, 2, 512, 4, 16, ctypes.byref(n)) == \
+        _native.ERR_UNSUPPORTED
+
+
+def test_path_selection_table():
+    lib = _native.library()
+    p = ctypes.c_int()
+    expect = {(128, 4, 32): 1, (128, 2, 32): 1, (64, 4, 16): 1, (256, 4, 64): 1, (128, 4, 128): 1,
+              (32, 4, 16): 2, (128, 4, 8): 2, (96, 4, 32): 2, (64, 2, 64): 1}
+    for (d, bits, group), path in expect.items():
+        assert lib.kvssd_b200_decode_path(d, bits, group, ctypes.byref(p)) == 0
+        assert p.value == path, (d, bits, group)
+    assert lib.kvssd_b200_set_path_override(2) == 0
+    lib.kvssd_b200_decode_path(128, 4, 32, ctypes.byref(p))
+    assert p.value == 2
+    assert lib.kvssd_b200_set_path_override(1) == 0
+    assert lib.kvssd_b200_decode_path(32, 4, 16, ctypes.byref(p)) == _native.ERR_UNSUPPORTED
+    assert lib.kvssd_b200_set_path_override(0) == 0
+    assert lib.kvssd_b200_set_path_override(7) == _native.ERR_INVALID_ARGUMENT
+
+
+def test_merge_and_dequant_argument_checks():
+    lib = _native.library()
+    assert lib.kvssd_b200_merge_chunks(None, None, 2, 4, 8, None, None, None) == _native.ERR_INVALID_ARGUMENT
+    assert lib.kvssd_b200_merge_pair(None, None, None, None, 4, 8, None, None, None) == \
+        _native.ERR_INVALID_ARGUMENT
+    dummy = ctypes.c_void_p(16)
+    assert lib.kvssd_b200_dequantize(dummy, dummy, 4, 128, 3, 32, 0, dummy, dummy, None) == \
+        _native.ERR_INVALID_ARGUMENT
+    assert lib.kvssd_b200_dequantize(dummy, dummy, 3, 128, 4, 32, 1, dummy, dummy, None) == \
+        _native.ERR_INVALID_ARGUMENT
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path: Path):
+    monkeypatch.setattr(_native, "LIB_PATH", tmp_path / "absent.so")
+    monkeypatch.setattr(_native, "_lib", None)
+    with pytest.raises(RuntimeError, match="not built"):
+        _native.library()
+    assert not _native.available()
