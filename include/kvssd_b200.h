@@ -55,8 +55,11 @@ enum kvssd_b200_query_dtype {
 /* Decode kernel selection, reported by kvssd_b200_decode_path and settable for A/B runs. */
 enum kvssd_b200_path {
   KVSSD_B200_PATH_AUTO = 0,
-  KVSSD_B200_PATH_TENSOR_CORE = 1, /* mma.sync split-KV kernel (head_dim 64/128/256, group>=16) */
-  KVSSD_B200_PATH_GENERIC = 2      /* CUDA-core split-KV kernel (any head_dim <= 256) */
+  KVSSD_B200_PATH_TENSOR_CORE = 1,     /* mma.sync split-KV tile math (head_dim 64/128/256,
+                                          group >= 16); TMA-fed where the layout qualifies */
+  KVSSD_B200_PATH_GENERIC = 2,         /* CUDA-core split-KV kernel (any head_dim <= 256) */
+  KVSSD_B200_PATH_TENSOR_CORE_REGS = 3 /* override only: tensor-core tile math fed by
+                                          per-thread global loads (no TMA ring) */
 };
 
 /* Library ABI version (incremented on any signature change). No reference counterpart. */
@@ -109,6 +112,13 @@ KVSSD_B200_API int kvssd_b200_decode_combine(const void* workspace, int n_parts,
 /* Which decode kernel kvssd_b200_decode would run for this geometry (KVSSD_B200_PATH_*).
  * No reference counterpart (the reference has one kernel). */
 KVSSD_B200_API int kvssd_b200_decode_path(int head_dim, int bits, int group_size, int* path);
+
+/* Launch plan kvssd_b200_decode would use on the current device for 16-byte aligned operands:
+ * *kernel = KVSSD_B200_PATH_TENSOR_CORE (TMA-fed), _TENSOR_CORE_REGS or _GENERIC; the number of
+ * split CTAs and of (m, l, acc) parts. No reference counterpart. */
+KVSSD_B200_API int kvssd_b200_decode_plan(int n_sel_blocks, int block_tokens, int query_heads,
+                                          int kv_heads, int head_dim, int bits, int group_size,
+                                          int* kernel, int* n_splits, int* n_parts);
 
 /* Process-wide override of the decode kernel choice (KVSSD_B200_PATH_*), for A/B
  * measurements and tests; AUTO restores the default. No reference counterpart. */

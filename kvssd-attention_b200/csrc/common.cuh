@@ -29,6 +29,7 @@ enum QueryDtype : int { kQF32 = 0, kQF16 = 1, kQBF16 = 2, kQF64 = 3 };
 enum DeviceStatusBits : unsigned {
   kDevBadBlockIndex = 1u,   // a block-table entry outside [0, n_pool_blocks)
   kDevBadValidCount = 2u,   // a valid_tokens entry outside [0, block_tokens]
+  kDevPipelineTimeout = 4u, // a bounded wait inside a pipelined kernel gave up
 };
 
 __device__ __forceinline__ float load_query(const void* q, int dtype, long long idx) {
@@ -183,6 +184,44 @@ struct VecBytes<2> {
     unsigned short s;
     asm("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(s) : "l"(p));
     w[0] = s;
+  }
+};
+
+template <int N>
+struct LdsBytes;  // shared-memory loads of N contiguous bytes into 32-bit words
+
+template <>
+struct LdsBytes<32> {
+  __device__ __forceinline__ static void load(const uint8_t* p, uint32_t* w) {
+    const uint4 a = reinterpret_cast<const uint4*>(p)[0], b = reinterpret_cast<const uint4*>(p)[1];
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+    w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+  }
+};
+template <>
+struct LdsBytes<16> {
+  __device__ __forceinline__ static void load(const uint8_t* p, uint32_t* w) {
+    const uint4 a = *reinterpret_cast<const uint4*>(p);
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  }
+};
+template <>
+struct LdsBytes<8> {
+  __device__ __forceinline__ static void load(const uint8_t* p, uint32_t* w) {
+    const uint2 a = *reinterpret_cast<const uint2*>(p);
+    w[0] = a.x; w[1] = a.y;
+  }
+};
+template <>
+struct LdsBytes<4> {
+  __device__ __forceinline__ static void load(const uint8_t* p, uint32_t* w) {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  }
+};
+template <>
+struct LdsBytes<2> {
+  __device__ __forceinline__ static void load(const uint8_t* p, uint32_t* w) {
+    w[0] = *reinterpret_cast<const unsigned short*>(p);
   }
 };
 

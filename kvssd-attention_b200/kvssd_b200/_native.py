@@ -20,7 +20,7 @@ ERR_CUDA = 4
 ERR_DEVICE_STATUS = 5
 
 Q_F32, Q_F16, Q_BF16, Q_F64 = 0, 1, 2, 3
-PATH_AUTO, PATH_TENSOR_CORE, PATH_GENERIC = 0, 1, 2
+PATH_AUTO, PATH_TENSOR_CORE, PATH_GENERIC, PATH_TENSOR_CORE_REGS = 0, 1, 2, 3
 
 _c_int = ctypes.c_int
 _c_ll = ctypes.c_longlong
@@ -60,6 +60,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "kvssd_b200_decode_combine": (_c_int, [_c_void, _c_int, _c_int, _c_int, _c_void, _c_void, _c_void]),
     "kvssd_b200_decode_path": (_c_int, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
+    "kvssd_b200_decode_plan": (
+        _c_int, [_c_int] * 7 + [ctypes.POINTER(_c_int)] * 3
+    ),
     "kvssd_b200_set_path_override": (_c_int, [_c_int]),
     "kvssd_b200_read_status": (_c_int, [_c_void, _c_int, _c_uint_p, _c_void]),
     "kvssd_b200_merge_chunks": (

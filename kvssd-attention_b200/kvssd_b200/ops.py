@@ -232,6 +232,22 @@ def decode_path(head_dim: int, bits: int, group_size: int) -> int:
     return path.value
 
 
+def decode_plan(n_sel: int, block_tokens: int, query_heads: int, kv_heads: int, head_dim: int,
+                bits: int, group_size: int) -> dict:
+    """Kernel choice and split count for a geometry on the current CUDA device."""
+    kernel, splits, parts = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    _native.check(
+        _native.library().kvssd_b200_decode_plan(
+            n_sel, block_tokens, query_heads, kv_heads, head_dim, bits, group_size,
+            ctypes.byref(kernel), ctypes.byref(splits), ctypes.byref(parts)),
+        "kvssd_b200_decode_plan",
+    )
+    names = {_native.PATH_TENSOR_CORE: "tensor_core_tma",
+             _native.PATH_TENSOR_CORE_REGS: "tensor_core_regs", _native.PATH_GENERIC: "generic"}
+    return {"kernel": names[kernel.value], "path": kernel.value, "n_splits": splits.value,
+            "n_parts": parts.value}
+
+
 def set_path_override(path: int) -> None:
     _native.check(_native.library().kvssd_b200_set_path_override(path), "set_path_override")
 
