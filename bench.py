@@ -51,6 +51,8 @@ def parse_args():
     ap.add_argument("--copies", type=int, default=3,
                     help="input copies rotated between steps so no step reads from L2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", choices=["auto", "stream", "regs", "generic"], default="auto",
+                    help="A/B: force the cp.async-streamed, register-fed or CUDA-core decode kernel")
     ap.add_argument("--kernel-only", action="store_true",
                     help="profiling aid: only the device-timed decode loop (no roofline leg, "
                          "e2e leg or CPU baseline)")
@@ -205,6 +207,10 @@ def run_ours(args) -> None:
                          "launch with torch.distributed.run")
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    from kvssd_b200 import _native
+    ops.set_path_override({"auto": _native.PATH_AUTO, "stream": _native.PATH_TENSOR_CORE,
+                           "regs": _native.PATH_TENSOR_CORE_REGS,
+                           "generic": _native.PATH_GENERIC}[args.path])
     dist = None
     if world > 1:
         import torch.distributed as dist
@@ -285,7 +291,8 @@ def run_ours(args) -> None:
             dist.destroy_process_group()
         if rank == 0:
             print(json.dumps({"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
-                              "steps": args.steps, "ms_per_step": ms, "kernel_only": True}))
+                              "steps": args.steps, "ms_per_step": ms, "kernel_only": True,
+                              "path": args.path}))
         return
 
     # ---- roofline leg: the streaming split-KV kernel alone, same inputs and rotation
@@ -297,7 +304,7 @@ def run_ours(args) -> None:
     kernel_ms = timed(split_only, args.steps, 3)
     plan = ops.decode_plan(w.blocks_per_layer, w.block_tokens, w.query_heads, w.kv_heads,
                            w.head_dim, w.bits, w.group_size)
-    kernel_name = {"tensor_core_tma": "tma_decode_kernel", "tensor_core_regs": "tc_decode_kernel",
+    kernel_name = {"tensor_core_stream": "async_decode_kernel", "tensor_core_regs": "tc_decode_kernel",
                    "generic": "simt_decode_kernel"}[plan["kernel"]]
     peak, peak_kind = peaks()
     achieved = nbytes / (kernel_ms * 1e-3) / 1e9

@@ -56,10 +56,10 @@ enum kvssd_b200_query_dtype {
 enum kvssd_b200_path {
   KVSSD_B200_PATH_AUTO = 0,
   KVSSD_B200_PATH_TENSOR_CORE = 1,     /* mma.sync split-KV tile math (head_dim 64/128/256,
-                                          group >= 16); TMA-fed where the layout qualifies */
+                                          group >= 16); cp.async-streamed where it qualifies */
   KVSSD_B200_PATH_GENERIC = 2,         /* CUDA-core split-KV kernel (any head_dim <= 256) */
   KVSSD_B200_PATH_TENSOR_CORE_REGS = 3 /* override only: tensor-core tile math fed by
-                                          per-thread global loads (no TMA ring) */
+                                          per-thread global loads (no shared-memory ring) */
 };
 
 /* Library ABI version (incremented on any signature change). No reference counterpart. */
@@ -114,7 +114,7 @@ KVSSD_B200_API int kvssd_b200_decode_combine(const void* workspace, int n_parts,
 KVSSD_B200_API int kvssd_b200_decode_path(int head_dim, int bits, int group_size, int* path);
 
 /* Launch plan kvssd_b200_decode would use on the current device for 16-byte aligned operands:
- * *kernel = KVSSD_B200_PATH_TENSOR_CORE (TMA-fed), _TENSOR_CORE_REGS or _GENERIC; the number of
+ * *kernel = KVSSD_B200_PATH_TENSOR_CORE (streamed), _TENSOR_CORE_REGS or _GENERIC; the number of
  * split CTAs and of (m, l, acc) parts. No reference counterpart. */
 KVSSD_B200_API int kvssd_b200_decode_plan(int n_sel_blocks, int block_tokens, int query_heads,
                                           int kv_heads, int head_dim, int bits, int group_size,

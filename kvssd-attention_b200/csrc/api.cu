@@ -22,10 +22,11 @@ namespace kvb {
 using DecodeKernel = void (*)(const DecodeArgs);
 DecodeKernel tc_decode_kernel_for(int bits, int d, int group);
 DecodeKernel simt_decode_kernel_for(int d);
-using TmaKernel = void (*)(const DecodeArgs, const TmaMaps);
-TmaKernel tma_decode_kernel_for(int bits, int d, int group);
-int tma_threads();
-int tma_warps();
+DecodeKernel async_decode_kernel_for(int bits, int d, int group);
+int async_threads();
+int async_warps();
+int async_depth();
+int async_stage_bytes(int group);
 using DequantKernel = void (*)(const uint8_t*, const __half*, long long, int, int, __half*,
                                uint8_t*);
 DequantKernel dequant_kernel_for(int bits, int mode);
@@ -109,11 +110,8 @@ int check_geometry(const Geometry& g) {
 
 struct Plan {
   int path = 0;
-  bool tma = false;
+  bool streaming = false;  // cp.async-fed kernel with per-warp shared-memory rings
   size_t smem = 0;
-  int stages = 0, stage_bytes = 0, ring_offset = 0, srb = 0;
-  int off_v = 0, off_ks = 0, off_vs = 0;
-  TmaKernel tma_kernel = nullptr;
   DecodeKernel kernel = nullptr;
   int gqa = 0, n_qsub = 0, n_vheads = 0, heads_per_cta = 0, wph = 0, n_head_groups = 0;
   int threads = 0, n_splits = 0, n_parts = 0, tiles_per_block = 0;
@@ -132,67 +130,20 @@ int choose_path(int d, int bits, int group) {
 
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
-// Shared-memory ring layout of the TMA-fed kernel; false if the geometry does not qualify
-// (INT4, head_dim 128, group >= 32, an even number of KV heads dividing the 16 warps, at most
-// 8 query heads per KV head, 16-byte scale rows, row indices within int32).
-bool plan_tma(const Geometry& g, long long pool_rows, const DeviceInfo& info, Plan& p) {
-  p.tma_kernel = tma_decode_kernel_for(g.bits, g.d, g.group);
-  if (p.tma_kernel == nullptr) return false;
-  if (p.n_qsub != 1 || g.kvh % 2 || tma_warps() % g.kvh) return false;
-  if (pool_rows >= (1LL << 31)) return false;
-  const int G = g.d / g.group;
-  p.srb = g.kvh * G * 2;
-  if (p.srb % 16) return false;
-  const int box_bytes = 16 * 128;
-  p.off_v = (g.kvh / 2) * box_bytes;
-  p.off_ks = 2 * p.off_v;
-  p.off_vs = p.off_ks + 16 * p.srb;
-  p.stage_bytes = round_up(p.off_vs + 16 * p.srb, 1024);
-  const int budget = info.max_smem_optin - 2048;
-  p.stages = std::min(16, budget / p.stage_bytes);
-  if (p.stages < 3) return false;
-  p.ring_offset = round_up(p.stages * 20, 1024);
-  if (p.ring_offset + p.stages * p.stage_bytes > budget) --p.stages;
-  const int merge_bytes = (tma_warps() - g.kvh) * 32 * (4 + 4 * (g.d / 16)) * 4;
-  if (p.stages < 3 || merge_bytes > p.stages * p.stage_bytes) return false;
-  p.smem = 1024 + static_cast<size_t>(p.ring_offset) + static_cast<size_t>(p.stages) * p.stage_bytes;
-  return true;
+// Shared memory of the streaming kernel (a private cp.async ring per warp); false if the
+// geometry does not qualify (INT4, head_dim 128, group 32 or 64, KV heads dividing the 16
+// warps, at most 8 query heads per KV head).
+bool plan_streaming(const Geometry& g, const DeviceInfo& info, Plan& p) {
+  p.kernel = async_decode_kernel_for(g.bits, g.d, g.group);
+  if (p.kernel == nullptr) return false;
+  if (p.n_qsub != 1 || async_warps() % g.kvh) return false;
+  p.smem = static_cast<size_t>(async_warps()) * async_depth() * async_stage_bytes(g.group);
+  const size_t merge_bytes = static_cast<size_t>(async_warps() - g.kvh) * 32 * (4 + 4 * (g.d / 16)) * 4;
+  return p.smem <= static_cast<size_t>(info.max_smem_optin) - 1024 && merge_bytes <= p.smem;
 }
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_tiled_fn() {
-  static EncodeTiledFn fn = [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
-            cudaSuccess || q != cudaDriverEntryPointSuccess) {
-      cudaGetLastError();
-      return static_cast<EncodeTiledFn>(nullptr);
-    }
-    return reinterpret_cast<EncodeTiledFn>(f);
-  }();
-  return fn;
-}
-
-// [rows][row_bytes] uint8 view, box 128 bytes x 16 rows, 128-byte swizzle, zero fill.
-bool encode_rows_map(CUtensorMap* map, const void* base, long long rows, int row_bytes) {
-  EncodeTiledFn fn = encode_tiled_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-  const cuuint32_t box[2] = {128, 16};
-  const cuuint32_t elem[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
-            elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// aligned: packed K/V 16-byte aligned; allow_tma: scales 16-byte aligned as well.
-int make_plan(const Geometry& g, bool aligned, bool allow_tma, Plan& p, long long pool_rows = 0) {
+// aligned: packed K/V 16-byte aligned; allow_stream: scales 16-byte aligned as well.
+int make_plan(const Geometry& g, bool aligned, bool allow_stream, Plan& p) {
   int st = check_geometry(g);
   if (st) return st;
   int dev = 0;
@@ -210,11 +161,11 @@ int make_plan(const Geometry& g, bool aligned, bool allow_tma, Plan& p, long lon
   p.gqa = g.qh / g.kvh;
   p.n_qsub = (p.gqa + 7) / 8;
   p.n_vheads = g.kvh * p.n_qsub;
-  if (p.path == KVSSD_B200_PATH_TENSOR_CORE && aligned && allow_tma &&
-      g_path_override != KVSSD_B200_PATH_TENSOR_CORE_REGS && plan_tma(g, pool_rows, info, p)) {
-    p.tma = true;
+  if (p.path == KVSSD_B200_PATH_TENSOR_CORE && aligned && allow_stream &&
+      g_path_override != KVSSD_B200_PATH_TENSOR_CORE_REGS && plan_streaming(g, info, p)) {
+    p.streaming = true;
     p.heads_per_cta = g.kvh;
-    p.wph = tma_warps() / g.kvh;
+    p.wph = async_warps() / g.kvh;
   } else if (p.path == KVSSD_B200_PATH_TENSOR_CORE) {
     p.kernel = tc_decode_kernel_for(g.bits, g.d, g.group);
     p.heads_per_cta = std::min(p.n_vheads, 8);
@@ -224,16 +175,16 @@ int make_plan(const Geometry& g, bool aligned, bool allow_tma, Plan& p, long lon
     p.heads_per_cta = 1;
     p.wph = 4;
   }
-  p.threads = p.tma ? tma_threads() : 32 * p.heads_per_cta * p.wph;
+  p.threads = p.streaming ? async_threads() : 32 * p.heads_per_cta * p.wph;
   p.n_head_groups = (p.n_vheads + p.heads_per_cta - 1) / p.heads_per_cta;
   p.tiles_per_block = (g.bt + 15) / 16;
   p.total_tiles = static_cast<long long>(g.n_sel) * p.tiles_per_block;
   const long long resident =
-      p.tma ? info.sms
+      p.streaming ? info.sms
             : static_cast<long long>(info.sms) * occupancy(p.kernel, p.threads) / p.n_head_groups;
   const long long by_work = (p.total_tiles + 2 * p.wph - 1) / (2 * p.wph);
   long long splits = std::max(1LL, std::min(resident, by_work));
-  const int parts_per_split = p.tma ? 1 : p.wph;  // the TMA kernel merges its warps in-CTA
+  const int parts_per_split = p.streaming ? 1 : p.wph;  // merged in-CTA by the streaming kernel
   splits = std::min<long long>(splits, kMaxParts / parts_per_split);
   p.n_splits = static_cast<int>(splits);
   p.n_parts = p.n_splits * parts_per_split;
@@ -318,7 +269,7 @@ int kvssd_b200_decode_plan(int n_sel_blocks, int block_tokens, int query_heads, 
   const int st = make_plan(g, true, true, p);
   if (st) return st;
   *kernel = p.path == KVSSD_B200_PATH_GENERIC ? KVSSD_B200_PATH_GENERIC
-                                              : (p.tma ? KVSSD_B200_PATH_TENSOR_CORE
+                                              : (p.streaming ? KVSSD_B200_PATH_TENSOR_CORE
                                                        : KVSSD_B200_PATH_TENSOR_CORE_REGS);
   *n_splits = p.n_splits;
   *n_parts = p.n_parts;
@@ -343,7 +294,7 @@ int prepare_decode(const void* query, int query_dtype, const uint8_t* packed_k,
                    const int32_t* valid_tokens, const int32_t* block_table, int n_pool_blocks,
                    int n_sel_blocks, int block_tokens, int query_heads, int kv_heads,
                    int head_dim, int bits, int group_size, float sm_scale, void* workspace,
-                   size_t workspace_bytes, DecodeArgs& a, Plan& p, TmaMaps& maps) {
+                   size_t workspace_bytes, DecodeArgs& a, Plan& p) {
   if (!query || !packed_k || !packed_v || !scales_k || !scales_v || !valid_tokens)
     return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "tensor pointers must not be NULL");
   if (query_dtype < KVSSD_B200_Q_F32 || query_dtype > KVSSD_B200_Q_F64)
@@ -355,19 +306,9 @@ int prepare_decode(const void* query, int query_dtype, const uint8_t* packed_k,
   if ((reinterpret_cast<uintptr_t>(scales_k) | reinterpret_cast<uintptr_t>(scales_v)) & 1u)
     return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "scales must be 2-byte aligned");
   const Geometry g{n_sel_blocks, block_tokens, query_heads, kv_heads, head_dim, bits, group_size};
-  const bool kv_aligned = aligned16(packed_k) && aligned16(packed_v);
-  const long long pool_rows = static_cast<long long>(n_pool_blocks) * block_tokens;
-  int st = make_plan(g, kv_aligned, aligned16(scales_k) && aligned16(scales_v), p, pool_rows);
+  int st = make_plan(g, aligned16(packed_k) && aligned16(packed_v),
+                     aligned16(scales_k) && aligned16(scales_v), p);
   if (st) return st;
-  if (p.tma) {
-    const int row_bytes = kv_heads * head_dim * bits / 8;
-    if (!encode_rows_map(&maps.k, packed_k, pool_rows, row_bytes) ||
-        !encode_rows_map(&maps.v, packed_v, pool_rows, row_bytes)) {
-      p = Plan();  // the driver refused the tensor maps: use the register-fed kernel
-      st = make_plan(g, kv_aligned, false, p, pool_rows);
-      if (st) return st;
-    }
-  }
   if (!workspace || workspace_bytes < p.ws_bytes)
     return fail(KVSSD_B200_ERR_WORKSPACE, "workspace needs " + std::to_string(p.ws_bytes) + " bytes");
   if (reinterpret_cast<uintptr_t>(workspace) & 15u)
@@ -397,13 +338,6 @@ int prepare_decode(const void* query, int query_dtype, const uint8_t* packed_k,
   a.total_tiles = p.total_tiles;
   a.n_splits = p.n_splits;
   a.score_scale = sm_scale * 1.4426950408889634f;  // log2(e): scores kept in log2 units
-  a.stages = p.stages;
-  a.stage_bytes = p.stage_bytes;
-  a.ring_offset = p.ring_offset;
-  a.srb = p.srb;
-  a.off_v = p.off_v;
-  a.off_ks = p.off_ks;
-  a.off_vs = p.off_vs;
   char* ws = static_cast<char*>(workspace);
   a.status = reinterpret_cast<unsigned*>(ws);
   a.part_ml = reinterpret_cast<float*>(ws + kHeaderBytes);
@@ -411,15 +345,13 @@ int prepare_decode(const void* query, int query_dtype, const uint8_t* packed_k,
   return KVSSD_B200_OK;
 }
 
-int launch_split(const DecodeArgs& a, const Plan& p, const TmaMaps& maps, cudaStream_t s) {
-  if (p.tma) {
-    cudaError_t e = cudaFuncSetAttribute(p.tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+int launch_split(const DecodeArgs& a, const Plan& p, cudaStream_t s) {
+  if (p.smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(p.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(p.smem));
     if (e != cudaSuccess) return cuda_fail(e, "shared-memory attribute");
-    p.tma_kernel<<<dim3(p.n_splits, 1, 1), dim3(p.threads, 1, 1), p.smem, s>>>(a, maps);
-  } else {
-    p.kernel<<<dim3(p.n_splits, p.n_head_groups, 1), dim3(p.threads, 1, 1), 0, s>>>(a);
   }
+  p.kernel<<<dim3(p.n_splits, p.n_head_groups, 1), dim3(p.threads, 1, 1), p.smem, s>>>(a);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "decode launch");
 }
@@ -439,14 +371,13 @@ int kvssd_b200_decode(const void* query, int query_dtype, const uint8_t* packed_
   if (!out || !lse) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "tensor pointers must not be NULL");
   DecodeArgs a;
   Plan p;
-  TmaMaps maps;
   int st = prepare_decode(query, query_dtype, packed_k, packed_v, scales_k, scales_v, valid_tokens,
                           block_table, n_pool_blocks, n_sel_blocks, block_tokens, query_heads,
                           kv_heads, head_dim, bits, group_size, sm_scale, workspace,
-                          workspace_bytes, a, p, maps);
+                          workspace_bytes, a, p);
   if (st) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  st = launch_split(a, p, maps, s);
+  st = launch_split(a, p, s);
   if (st) return st;
   cudaError_t e = launch_combine(a.part_acc, a.part_ml, p.n_parts, query_heads, head_dim, out, lse, s);
   return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "combine launch");
@@ -462,14 +393,13 @@ int kvssd_b200_decode_split(const void* query, int query_dtype, const uint8_t* p
   if (!n_parts) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "n_parts must not be NULL");
   DecodeArgs a;
   Plan p;
-  TmaMaps maps;
   int st = prepare_decode(query, query_dtype, packed_k, packed_v, scales_k, scales_v, valid_tokens,
                           block_table, n_pool_blocks, n_sel_blocks, block_tokens, query_heads,
                           kv_heads, head_dim, bits, group_size, sm_scale, workspace,
-                          workspace_bytes, a, p, maps);
+                          workspace_bytes, a, p);
   if (st) return st;
   *n_parts = p.n_parts;
-  return launch_split(a, p, maps, reinterpret_cast<cudaStream_t>(stream));
+  return launch_split(a, p, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int kvssd_b200_decode_combine(const void* workspace, int n_parts, int query_heads, int head_dim,

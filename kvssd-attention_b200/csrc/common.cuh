@@ -29,7 +29,6 @@ enum QueryDtype : int { kQF32 = 0, kQF16 = 1, kQBF16 = 2, kQF64 = 3 };
 enum DeviceStatusBits : unsigned {
   kDevBadBlockIndex = 1u,   // a block-table entry outside [0, n_pool_blocks)
   kDevBadValidCount = 2u,   // a valid_tokens entry outside [0, block_tokens]
-  kDevPipelineTimeout = 4u, // a bounded wait inside a pipelined kernel gave up
 };
 
 __device__ __forceinline__ float load_query(const void* q, int dtype, long long idx) {
@@ -144,6 +143,50 @@ __device__ __forceinline__ uint32_t transpose_8x8(uint32_t x) {
   uint32_t y;
   asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
   return y;
+}
+
+// Four 8x8 b16 matrices from shared memory; lane i supplies the address of row i%8 of matrix
+// i/8 (PTX ldmatrix). The .trans form hands thread (g, c) elements [2c][g] and [2c+1][g].
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                              uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 16-byte asynchronous global -> shared copy, cached in L2 only (PTX cp.async.cg).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// 8-byte asynchronous global -> shared copy (PTX cp.async.ca; 8-byte aligned addresses).
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// 4-byte asynchronous global -> shared copy (PTX cp.async.ca; 4-byte aligned addresses).
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 template <int N>

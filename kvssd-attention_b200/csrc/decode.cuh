@@ -12,18 +12,10 @@
 //     "part" of the split-KV result; part = split * wph + warp-subindex.
 #pragma once
 
-#include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
 namespace kvb {
-
-// Tensor maps of the TMA-fed kernel: the K and V pools viewed as 2-D [n_pool*bt token rows]
-// x [kv_heads*packed_dim bytes], box 128 bytes x 16 rows, 128-byte swizzle.
-struct TmaMaps {
-  CUtensorMap k;
-  CUtensorMap v;
-};
 
 struct DecodeArgs {
   const void* q;
@@ -44,12 +36,6 @@ struct DecodeArgs {
   long long total_tiles;
   int n_splits;
   float score_scale;  // sm_scale * log2(e): scores are kept in the log2 domain
-  // Shared-memory ring of the TMA-fed kernel (bytes); unused by the other kernels.
-  int stages;         // ring depth (tiles in flight per CTA)
-  int stage_bytes;    // one stage: 16 rows of K codes, V codes, K scales and V scales
-  int ring_offset;    // start of the ring after the mbarriers (1024-aligned)
-  int srb;            // global bytes of one token row of scales, all KV heads (kvh * G * 2)
-  int off_v, off_ks, off_vs;  // region offsets within a stage
   float* part_acc;    // [n_parts, qh, d] unnormalised sum p*v
   float* part_ml;     // [n_parts, qh, 2]  (running max in log2 domain, sum of p)
   unsigned* status;   // device status word (DeviceStatusBits)

@@ -242,7 +242,7 @@ def decode_plan(n_sel: int, block_tokens: int, query_heads: int, kv_heads: int, 
             ctypes.byref(kernel), ctypes.byref(splits), ctypes.byref(parts)),
         "kvssd_b200_decode_plan",
     )
-    names = {_native.PATH_TENSOR_CORE: "tensor_core_tma",
+    names = {_native.PATH_TENSOR_CORE: "tensor_core_stream",
              _native.PATH_TENSOR_CORE_REGS: "tensor_core_regs", _native.PATH_GENERIC: "generic"}
     return {"kernel": names[kernel.value], "path": kernel.value, "n_splits": splits.value,
             "n_parts": parts.value}

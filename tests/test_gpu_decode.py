@@ -79,7 +79,7 @@ def test_tensor_core_path_covers_benchmark_shapes():
     for bits in (2, 4):
         assert ops.decode_path(128, bits, 32) == _native.PATH_TENSOR_CORE
     plan = ops.decode_plan(1024, 128, 32, 8, 128, 4, 32)  # the 128K-token INT4 configuration
-    assert plan["kernel"] == "tensor_core_tma", plan
+    assert plan["kernel"] == "tensor_core_stream", plan
     assert plan["n_parts"] == plan["n_splits"] <= sms
     assert ops.decode_plan(33, 128, 32, 8, 128, 2, 32)["kernel"] == "tensor_core_regs"
 
@@ -89,7 +89,7 @@ def test_tensor_core_path_covers_benchmark_shapes():
 @pytest.mark.parametrize("kvh,qh,bits", [(8, 32, 4), (8, 32, 2), (4, 16, 4), (2, 16, 4),
                                          (1, 8, 4), (8, 8, 4), (16, 32, 4)])
 def test_kernels_agree_with_oracle_across_head_layouts(kvh, qh, bits, path, path_override):
-    """Every decode kernel against the oracle for KV-head counts that change the TMA ring
+    """Every decode kernel against the oracle for KV-head counts that change the streaming ring
     layout (row bytes 64..1024) and the warps-per-head split, including partial tiles."""
     pool = _pool(nb=9, kvh=kvh, bits=bits, valid=[128, 128, 100, 128, 3, 128, 128, 64, 17])
     q = torch.randn(qh, 128, generator=torch.Generator().manual_seed(kvh * 100 + qh)).half()
