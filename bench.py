@@ -197,6 +197,7 @@ def run_reference(args) -> None:
 
 def run_ours(args) -> None:
     from kvssd_b200 import B200AttentionBackend, PackedBatch, ops
+    from kvssd_b200.sharding import ShardedDecoder
     from kvssd_b200.workloads import WORKLOADS, make_layer
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -229,22 +230,21 @@ def run_ours(args) -> None:
     nbytes = w.blocks_per_layer * w.bytes_per_block
     qh, d = q.shape
     scale = 1 / math.sqrt(d)
-    send = torch.empty(qh * d + qh, dtype=torch.float32, device=device)
-    out_v, lse_v = send[: qh * d].view(qh, d), send[qh * d :]
-    recv = torch.empty((world, qh * d + qh), dtype=torch.float32, device=device)
-
-    def exchange_and_merge():
-        dist.all_gather_into_tensor(recv, send)
-        outs = recv[:, : qh * d].reshape(world, qh, d).contiguous()
-        lses = recv[:, qh * d :].contiguous()
-        return ops.merge_chunks(outs, lses)
+    out_v = torch.empty((qh, d), dtype=torch.float32, device=device)
+    lse_v = torch.empty((qh,), dtype=torch.float32, device=device)
+    batches = [PackedBatch(p.packed_k, p.packed_v, p.scales_k, p.scales_v, p.valid_tokens,
+                           w.bits, w.group_size) for p in pools]
+    # N > 1: this rank's 1024 blocks are its token-block shard of the N x 1024-block context;
+    # the library's ShardedDecoder decodes it, all-gathers (out, lse) over NCCL and merges.
+    sharded = ShardedDecoder("tokens") if world > 1 else None
 
     def step(i: int):
+        if sharded is not None:
+            sharded.run(q, batches[i % len(batches)], scale)
+            return
         p = pools[i % len(pools)]
         ops.decode(q, p.packed_k, p.packed_v, p.scales_k, p.scales_v, p.valid_tokens, w.bits,
                    w.group_size, scale, out=out_v, lse=lse_v)
-        if world > 1:
-            exchange_and_merge()
 
     stream = torch.cuda.current_stream(device)
 
@@ -326,11 +326,10 @@ def run_ours(args) -> None:
         for src, dst in zip(host, dev_bufs):
             dst.copy_(src, non_blocking=True)
         batch = PackedBatch(*dev_bufs[:5], w.bits, w.group_size)
-        out, lse = backend.run(dev_bufs[5], batch, scale)
-        if world > 1:
-            out_v.copy_(out)
-            lse_v.copy_(lse)
-            out, lse = exchange_and_merge()
+        if sharded is not None:
+            out, lse = sharded.run(dev_bufs[5], batch, scale)
+        else:
+            out, lse = backend.run(dev_bufs[5], batch, scale)
         out_host.copy_(out, non_blocking=True)
 
     e2e_steps = max(3, min(args.steps, 20))
@@ -370,7 +369,9 @@ def run_ours(args) -> None:
                      "kernel_us": kernel_ms * 1e3, "peak_kind": f"{peak_kind} (burst copy)"},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                "path": "B200AttentionBackend.run (C ABI) from pinned host buffers"},
+                "path": ("ShardedDecoder.run (C ABI decode, NCCL all-gather, merge kernel)"
+                         if world > 1 else "B200AttentionBackend.run (C ABI)")
+                        + " from pinned host buffers"},
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clock_summary,
     }

@@ -128,7 +128,6 @@ int choose_path(int d, int bits, int group) {
   return tc_ok ? KVSSD_B200_PATH_TENSOR_CORE : KVSSD_B200_PATH_GENERIC;
 }
 
-int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
 // Shared memory of the streaming kernel (a private cp.async ring per warp); false if the
 // geometry does not qualify (INT4, head_dim 128, group 32 or 64, KV heads dividing the 16

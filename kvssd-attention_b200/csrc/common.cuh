@@ -165,19 +165,33 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// L2 policy for data read exactly once: evicted first, so it does not push out data that is
+// reused soon (e.g. the split-KV parts the combine kernel reads next).
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
 // 16-byte asynchronous global -> shared copy, cached in L2 only (PTX cp.async.cg).
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst),
+               "l"(src), "l"(policy)
+               : "memory");
 }
 
 // 8-byte asynchronous global -> shared copy (PTX cp.async.ca; 8-byte aligned addresses).
-__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, uint64_t policy) {
+  asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 8, %2;" ::"r"(dst),
+               "l"(src), "l"(policy)
+               : "memory");
 }
 
 // 4-byte asynchronous global -> shared copy (PTX cp.async.ca; 4-byte aligned addresses).
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint64_t policy) {
+  asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 4, %2;" ::"r"(dst),
+               "l"(src), "l"(policy)
+               : "memory");
 }
 
 __device__ __forceinline__ void cp_async_commit() {

@@ -18,13 +18,18 @@
 //
 // Math (per warp, per tile of 16 tokens): with 32 dims per 16-byte chunk and group_size >= 32,
 // every k-step of QK and every M-tile of PV lies inside one scale group, so scales are applied
-// outside the tensor-core products, which multiply exact centred codes:
-//   QK: S[t,n] = sum_group sk[t,group] * (sum_{d in group} (code-mid)[t,d] * q[n,d])
-//       -- two m16n8k16 per group into a fresh FP32 accumulator, then one FFMA per element;
+// outside the tensor-core products:
+//   QK: S[t,n] = sum_group sk[t,group] * (sum_{d in group} (code-mid)[t,d] * q[n,d]);
+//       the codes enter the mma as the raw FP16 values 1024+n / 1024+16n (q pre-divided by 16
+//       for the latter); each group's FP32 accumulator starts at -C, C being the constant those
+//       encodings add (computed once by the same mma from constant rows), so it ends at the
+//       exact centred product; one FFMA per element then applies the K scale;
 //   PV: O^T[d,n] = sum_t (code-mid)[t,d] * (P[t,n] * sv[t,group(d)])
 //       -- the V scale is folded into the FP16 P operand of the M-tiles of that group;
 //   ldmatrix.trans delivers V with two tokens per 32-bit register, the pairing the PV A
-//   fragment needs. The online softmax runs in the log2 domain on the QK accumulator.
+//   fragment needs. The online softmax runs in the log2 domain (q pre-scaled by
+//   sm_scale*log2(e)) with a lazily updated running max: the max and the accumulator move only
+//   when a score exceeds the running max by 2^8, detected with one warp vote per tile.
 // The CTA finally merges the wph warps of each head through shared memory and writes one
 // (m, l, acc) part per query head for the combine kernel.
 #include "decode_tc.cuh"
@@ -49,6 +54,27 @@ struct ScaleRow {  // the G FP16 scales of one (token, KV head)
   }
 };
 
+// Raw K codes for the QK mma: (1024 + n) in the even and (1024 + 16n) in the odd code slots of
+// each 16-bit lane, two instructions fewer per pair than centring; the constant offsets are
+// cancelled exactly through the accumulator start value (see async_decode_kernel).
+__device__ __forceinline__ void magic_pairs(uint32_t x, uint32_t (&o)[4]) {
+  const uint32_t x8 = x >> 8;
+  o[0] = or_magic<0x000F000Fu>(x);
+  o[1] = or_magic<0x00F000F0u>(x);
+  o[2] = or_magic<0x000F000Fu>(x8);
+  o[3] = or_magic<0x00F000F0u>(x8);
+}
+
+// D = A * B with a zero accumulator start (no register moves for C).
+__device__ __forceinline__ void mma_16816_set(float (&d)[4], uint32_t a0, uint32_t a1,
+                                              uint32_t a2, uint32_t a3, uint32_t b0,
+                                              uint32_t b1, float c0, float c1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1));
+}
+
 template <int GROUP>
 __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const DecodeArgs a) {
   constexpr int D = 128, BITS = 4, G = D / GROUP, MT = D / 16, DEPTH = kAsyncDepth;
@@ -56,6 +82,7 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
   constexpr int SB = 2 * G;                   // scale bytes per (token, head)
   constexpr int OFF_V = 16 * PD, OFF_KS = 32 * PD, OFF_VS = OFF_KS + 16 * SB;
   constexpr int STAGE = ((OFF_VS + 16 * SB) + 127) / 128 * 128;
+  constexpr float kLazyMax = 8.f;  // rescale only when a score beats the running max by 2^8
   static_assert(G == 4 || G == 2, "scale rows must be whole 4-byte words");
   extern __shared__ __align__(128) uint8_t smem[];
   asm volatile("griddepcontrol.launch_dependents;");
@@ -72,12 +99,18 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
   const int n_mine = sub < n_tiles ? (n_tiles - sub + wph - 1) / wph : 0;
 
   // ---------------- feed: this warp's copies of its i-th tile into stage i % DEPTH
-  const size_t row_bytes = static_cast<size_t>(kvh) * PD;
-  const uint8_t* kp = a.kp + h * PD;
-  const uint8_t* vp = a.vp + h * PD;
-  const uint8_t* ksb = reinterpret_cast<const uint8_t*>(a.ks) + h * SB;
-  const uint8_t* vsb = reinterpret_cast<const uint8_t*>(a.vs) + h * SB;
-  const size_t srow = static_cast<size_t>(kvh) * SB;
+  // Lane (r, q) copies 16-byte chunk q of rows r and r+8 of K and V (chunk q of row r is stored
+  // at chunk q ^ ((r >> 1) & 3)); lanes 0-15 copy the K scale row, lanes 16-31 the V scale row.
+  const int row_bytes = kvh * PD;
+  const int srow = kvh * SB;
+  const int cr = lane >> 2, cq = lane & 3, sr = lane & 15;
+  const uint32_t dst_kv = cr * PD + ((cq ^ ((cr >> 1) & 3)) << 4);
+  const uint32_t dst_s = (lane < 16 ? OFF_KS : OFF_VS) + sr * SB;
+  const uint8_t* k_lane = a.kp + h * PD + cr * row_bytes + cq * 16;
+  const uint8_t* v_lane = a.vp + h * PD + cr * row_bytes + cq * 16;
+  const uint8_t* s_lane = reinterpret_cast<const uint8_t*>(lane < 16 ? a.ks : a.vs) + h * SB +
+                          sr * srow;
+  const uint64_t policy = l2_evict_first();
   BlockInfoCache cache;
   TileCursor cur;
   cur.seek(t_begin + sub, a.tiles_per_block);
@@ -92,27 +125,19 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
       if (lane == 0) tile_rows[warp][fill_slot] = rows;
       if (rows > 0) {
         const size_t row0 = static_cast<size_t>(blk) * a.bt + off;
+        const size_t kv_off = row0 * row_bytes, s_off = row0 * srow;
         const uint32_t st = ring_s + fill_slot * STAGE;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int r = (lane >> 2) + 8 * half, q = lane & 3;
-          if (r < rows) {
-            const uint32_t d = st + r * PD + ((q ^ ((r >> 1) & 3)) << 4);
-            const size_t src = (row0 + r) * row_bytes + q * 16;
-            cp_async16(d, kp + src);
-            cp_async16(d + OFF_V, vp + src);
-          }
+        if (cr < rows) {
+          cp_async16(st + dst_kv, k_lane + kv_off, policy);
+          cp_async16(st + OFF_V + dst_kv, v_lane + kv_off, policy);
         }
-        const int r = lane & 15;
-        if (r < rows) {
-          const size_t src = (row0 + r) * srow;
-          if (lane < 16) {
-            if constexpr (G == 4) cp_async8(st + OFF_KS + r * SB, ksb + src);
-            else cp_async4(st + OFF_KS + r * SB, ksb + src);
-          } else {
-            if constexpr (G == 4) cp_async8(st + OFF_VS + r * SB, vsb + src);
-            else cp_async4(st + OFF_VS + r * SB, vsb + src);
-          }
+        if (cr + 8 < rows) {
+          cp_async16(st + 8 * PD + dst_kv, k_lane + kv_off + 8 * row_bytes, policy);
+          cp_async16(st + OFF_V + 8 * PD + dst_kv, v_lane + kv_off + 8 * row_bytes, policy);
+        }
+        if (sr < rows) {
+          if constexpr (G == 4) cp_async8(st + dst_s, s_lane + s_off, policy);
+          else cp_async4(st + dst_s, s_lane + s_off, policy);
         }
       }
       if (++fill_slot == DEPTH) fill_slot = 0;
@@ -124,8 +149,9 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
 
   // ---------------- compute state
   const int q0 = h * a.gqa, nq = a.gqa;
-  // Q as the B operand: k-step (m, j2) of thread c covers dims 32m + 8c + {2j2, 2j2+4} (b0)
-  // and 32m + 8c + {2j2+1, 2j2+5} (b1), the order the ldmatrix/unpack path produces.
+  // Q (pre-multiplied by sm_scale*log2(e)) as the B operand: k-step (m, j2) of thread c covers
+  // dims 32m + 8c + {2j2, 2j2+4} (b0, even code slots) and 32m + 8c + {2j2+1, 2j2+5} (b1, odd
+  // code slots, divided by 16 to match the (1024 + 16n) encoding; exact power-of-two scaling).
   uint32_t qf[4][2][2];
 #pragma unroll
   for (int m = 0; m < 4; ++m)
@@ -137,20 +163,35 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
         float f0 = 0.f, f1 = 0.f;
         if (g < nq) {
           const long long qb = static_cast<long long>(q0 + g) * D;
-          f0 = load_query(a.q, a.q_dtype, qb + d0);
-          f1 = load_query(a.q, a.q_dtype, qb + d1);
+          const float sc = r ? a.score_scale * 0.0625f : a.score_scale;
+          f0 = load_query(a.q, a.q_dtype, qb + d0) * sc;
+          f1 = load_query(a.q, a.q_dtype, qb + d1) * sc;
         }
         qf[m][j2][r] = h2_as_u32(__floats2half2_rn(f0, f1));
       }
+  // Per group m and head column: the constant the raw encoding adds to the QK product,
+  // C = sum_even 1032 q + sum_odd 1152 q/16 -- computed with the same mma from constant A rows,
+  // so each group's accumulator starts at -C and ends at sum (code - 8) q exactly.
+  float cneg[4][2];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    float c4[4];
+    mma_16816_set(c4, 0x64086408u, 0x64086408u, 0x64806480u, 0x64806480u, qf[m][0][0],
+                  qf[m][0][1], 0.f, 0.f);
+    mma_16816(c4, 0x64086408u, 0x64086408u, 0x64806480u, 0x64806480u, qf[m][1][0], qf[m][1][1]);
+    cneg[m][0] = -c4[0];
+    cneg[m][1] = -c4[1];
+  }
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   float acc[MT][4];
 #pragma unroll
   for (int i = 0; i < MT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   // ldmatrix: lane supplies row (lane & 7) of the matrix for 16-byte chunk (lane >> 3), at its
-  // swizzled position; rows 8-15 repeat the pattern 512 bytes further.
+  // swizzled position; rows 8-15 repeat the pattern 8 rows further.
   const int ld_row = lane & 7, ld_chunk = lane >> 3;
   const uint32_t ld_off =
       static_cast<uint32_t>(ld_row * PD + ((ld_chunk ^ ((ld_row >> 1) & 3)) << 4));
+  const uint32_t sk_off = OFF_KS + g * SB, sv_off = OFF_VS + 2 * c * SB;
 
   int slot = 0;
 #pragma unroll 1
@@ -162,9 +203,20 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
     const uint8_t* sp = ring + slot * STAGE;
     uint32_t kA[4], kB[4], vA[4], vB[4];
     ScaleRow<G> sk0, sk1, sv[4];
-    if (rows > 0) {
-      ldsm_x4(st + ld_off, kA[0], kA[1], kA[2], kA[3]);                 // K tokens 0-7
-      ldsm_x4(st + ld_off + 8 * PD, kB[0], kB[1], kB[2], kB[3]);        // K tokens 8-15
+    if (rows == 16) {
+      ldsm_x4(st + ld_off, kA[0], kA[1], kA[2], kA[3]);               // K tokens 0-7
+      ldsm_x4(st + ld_off + 8 * PD, kB[0], kB[1], kB[2], kB[3]);      // K tokens 8-15
+      ldsm_x4_trans(st + OFF_V + ld_off, vA[0], vA[1], vA[2], vA[3]);
+      ldsm_x4_trans(st + OFF_V + ld_off + 8 * PD, vB[0], vB[1], vB[2], vB[3]);
+      sk0.load(sp + sk_off);
+      sk1.load(sp + sk_off + 8 * SB);
+      sv[0].load(sp + sv_off);
+      sv[1].load(sp + sv_off + SB);
+      sv[2].load(sp + sv_off + 8 * SB);
+      sv[3].load(sp + sv_off + 9 * SB);
+    } else if (rows > 0) {  // partial tile: rows past the valid count re-read the last one
+      ldsm_x4(st + ld_off, kA[0], kA[1], kA[2], kA[3]);
+      ldsm_x4(st + ld_off + 8 * PD, kB[0], kB[1], kB[2], kB[3]);
       ldsm_x4_trans(st + OFF_V + ld_off, vA[0], vA[1], vA[2], vA[3]);
       ldsm_x4_trans(st + OFF_V + ld_off + 8 * PD, vB[0], vB[1], vB[2], vB[3]);
       const int last = rows - 1;
@@ -180,41 +232,41 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
     if (++slot == DEPTH) slot = 0;
     if (rows <= 0) continue;
 
-    // ---- QK per scale group
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    // ---- QK per scale group: r4 = sum_group (code - 8) q, then scaled by the K scale
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
-      __half2 p0[4], p1[4];
-      LanePairs<BITS>::centred(kA[m], p0);
-      LanePairs<BITS>::centred(kB[m], p1);
-      float r4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int j2 = 0; j2 < 2; ++j2)
-        mma_16816(r4, h2_as_u32(p0[2 * j2]), h2_as_u32(p1[2 * j2]), h2_as_u32(p0[2 * j2 + 1]),
-                  h2_as_u32(p1[2 * j2 + 1]), qf[m][j2][0], qf[m][j2][1]);
+      uint32_t p0[4], p1[4];
+      magic_pairs(kA[m], p0);
+      magic_pairs(kB[m], p1);
+      float r4[4];
+      mma_16816_set(r4, p0[0], p1[0], p0[1], p1[1], qf[m][0][0], qf[m][0][1], cneg[m][0],
+                    cneg[m][1]);
+      mma_16816(r4, p0[2], p1[2], p0[3], p1[3], qf[m][1][0], qf[m][1][1]);
       const int gi = (32 * m) / GROUP;
       const float s0 = __half2float(sk0.s[gi]), s1 = __half2float(sk1.s[gi]);
-      sc[0] = fmaf(r4[0], s0, sc[0]);
-      sc[1] = fmaf(r4[1], s0, sc[1]);
-      sc[2] = fmaf(r4[2], s1, sc[2]);
-      sc[3] = fmaf(r4[3], s1, sc[3]);
+      x[0] = fmaf(r4[0], s0, x[0]);
+      x[1] = fmaf(r4[1], s0, x[1]);
+      x[2] = fmaf(r4[2], s1, x[2]);
+      x[3] = fmaf(r4[3], s1, x[3]);
     }
-    // ---- online softmax (log2 domain); rows g, g+8 x heads 2c, 2c+1
-    const bool v0 = g < rows, v1 = g + 8 < rows;
-    const float x0 = v0 ? sc[0] * a.score_scale : -INFINITY;
-    const float x1 = v0 ? sc[1] * a.score_scale : -INFINITY;
-    const float x2 = v1 ? sc[2] * a.score_scale : -INFINITY;
-    const float x3 = v1 ? sc[3] * a.score_scale : -INFINITY;
-    float t0 = fmaxf(x0, x2), t1 = fmaxf(x1, x3);
+    // ---- online softmax in the log2 domain; rows g, g+8 x heads 2c, 2c+1
+    if (rows < 16) {
+      if (g >= rows) x[0] = x[1] = -INFINITY;
+      if (g + 8 >= rows) x[2] = x[3] = -INFINITY;
+    }
+    // The running max moves only when some score exceeds it by kLazyMax: p stays <= 2^8.
+    const bool up = x[0] > m_run[0] + kLazyMax || x[2] > m_run[0] + kLazyMax ||
+                    x[1] > m_run[1] + kLazyMax || x[3] > m_run[1] + kLazyMax;
+    if (__any_sync(0xffffffffu, up)) {
+      float t0 = fmaxf(x[0], x[2]), t1 = fmaxf(x[1], x[3]);
 #pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
-      t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, o));
-    }
-    const float n0 = fmaxf(m_run[0], t0), n1 = fmaxf(m_run[1], t1);
-    const float u0 = n0 == -INFINITY ? 0.f : n0, u1 = n1 == -INFINITY ? 0.f : n1;
-    if (__any_sync(0xffffffffu, (n0 > m_run[0]) || (n1 > m_run[1]))) {
-      const float al0 = fast_exp2(m_run[0] - u0), al1 = fast_exp2(m_run[1] - u1);
+      for (int o = 4; o < 32; o <<= 1) {
+        t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
+        t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, o));
+      }
+      const float n0 = fmaxf(m_run[0], t0), n1 = fmaxf(m_run[1], t1);
+      const float al0 = fast_exp2(m_run[0] - n0), al1 = fast_exp2(m_run[1] - n1);
       l_run[0] *= al0;
       l_run[1] *= al1;
 #pragma unroll
@@ -224,11 +276,11 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
         acc[k][2] *= al0;
         acc[k][3] *= al1;
       }
+      m_run[0] = n0;
+      m_run[1] = n1;
     }
-    m_run[0] = n0;
-    m_run[1] = n1;
-    const float e0 = fast_exp2(x0 - u0), e1 = fast_exp2(x1 - u1);
-    const float e2 = fast_exp2(x2 - u0), e3 = fast_exp2(x3 - u1);
+    const float e0 = fast_exp2(x[0] - m_run[0]), e1 = fast_exp2(x[1] - m_run[1]);
+    const float e2 = fast_exp2(x[2] - m_run[0]), e3 = fast_exp2(x[3] - m_run[1]);
     l_run[0] += e0 + e2;
     l_run[1] += e1 + e3;
     const __half2 pt0 = u32_as_h2(transpose_8x8(h2_as_u32(__floats2half2_rn(e0, e1))));

@@ -1,0 +1,171 @@
+"""Multi-GPU decode: one process per GPU, the packed KV of a layer sharded two ways.
+
+* Token-block ranges (long contexts): rank r owns a contiguous, balanced range of the
+  selected blocks, decodes it into a normalised (out, lse) pair for every query head, and
+  the ranks exchange those pairs with one all-gather of ``query_heads * (head_dim + 1)``
+  FP32 values each; every rank then folds the N pairs with the exact N-way merge (the algebra
+  of kvssd's merge_attention_chunks, src/kvssd/attention.py:91-102, generalised to N).
+* KV-head groups (many layers, moderate contexts): rank r owns KV heads
+  ``[r*KVH/N, (r+1)*KVH/N)`` and the query heads mapped to them by kvssd's GQA rule
+  ``kv = h // (QH/KVH)`` (csrc/fused_decode.cu:34, backends/reference.py:41). No softmax
+  merge is needed: the ranks all-gather their output rows and LSEs and concatenate them in
+  rank order. kvssd records interleave heads per token (src/kvssd/format.py:165), so a
+  head shard is re-laid head-contiguous (``shard_batch_by_heads``) when it is staged.
+
+The exchange is a collective of the caller's process group (NCCL over NVLink for CUDA
+tensors). By default the local decode is libkvssd_b200's kernel writing straight into the
+send buffer and the merge is its N-way merge kernel; a ``decode_fn`` / ``merge_fn`` with the
+backend ``run`` / merge signatures can be injected instead (the host logic is the same).
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+from dataclasses import replace
+
+import torch
+import torch.distributed as dist
+
+from .backends.base import PackedBatch
+
+DecodeFn = Callable[[torch.Tensor, PackedBatch, float], tuple[torch.Tensor, torch.Tensor]]
+MergeFn = Callable[[torch.Tensor, torch.Tensor], tuple[torch.Tensor, torch.Tensor]]
+
+MODES = ("tokens", "heads")
+
+
+def block_range(n_blocks: int, rank: int, world: int) -> tuple[int, int]:
+    """Balanced contiguous block range [lo, hi) of ``rank`` (sizes differ by at most one)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if n_blocks < 0:
+        raise ValueError("n_blocks must be non-negative")
+    base, extra = divmod(n_blocks, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def head_shard(kv_heads: int, query_heads: int, rank: int, world: int) -> tuple[int, int, int, int]:
+    """(kv_lo, kv_hi, q_lo, q_hi) owned by ``rank``; KV heads must divide evenly over ranks."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if kv_heads % world:
+        raise ValueError(f"{kv_heads} KV heads do not divide over {world} ranks")
+    if query_heads % kv_heads:
+        raise ValueError("query heads must be divisible by KV heads")
+    per = kv_heads // world
+    gqa = query_heads // kv_heads
+    return rank * per, (rank + 1) * per, rank * per * gqa, (rank + 1) * per * gqa
+
+
+def shard_batch_by_blocks(batch: PackedBatch, rank: int, world: int) -> PackedBatch:
+    """The block-range shard of a stacked batch (views; no copy)."""
+    lo, hi = block_range(batch.packed_k.shape[0], rank, world)
+    return replace(batch, packed_k=batch.packed_k[lo:hi], packed_v=batch.packed_v[lo:hi],
+                   scales_k=batch.scales_k[lo:hi], scales_v=batch.scales_v[lo:hi],
+                   valid_tokens=batch.valid_tokens[lo:hi])
+
+
+def shard_batch_by_heads(batch: PackedBatch, rank: int, world: int,
+                         query_heads: int) -> PackedBatch:
+    """The KV-head shard of a stacked batch, re-laid head-contiguous (a copy)."""
+    kv_lo, kv_hi, _, _ = head_shard(batch.packed_k.shape[2], query_heads, rank, world)
+    cut = lambda t: t[:, :, kv_lo:kv_hi].contiguous()  # noqa: E731
+    return replace(batch, packed_k=cut(batch.packed_k), packed_v=cut(batch.packed_v),
+                   scales_k=cut(batch.scales_k), scales_v=cut(batch.scales_v))
+
+
+def _default_merge() -> MergeFn:
+    from . import ops
+
+    return ops.merge_chunks
+
+
+class ShardedDecoder:
+    """Decodes this rank's shard and returns the full (out fp32 [QH, D], lse fp32 [QH]) on
+    every rank of ``group``.
+
+    ``mode="tokens"``: ``local`` is this rank's block-range shard (it may hold no blocks,
+    which contributes an empty chunk: out 0, lse -inf). ``mode="heads"``: ``local`` is this
+    rank's KV-head shard and ``query`` the full query; the rank decodes its query heads.
+    All ranks take the same collective steps in the same order, whatever their shard holds.
+    """
+
+    def __init__(self, mode: str = "tokens", group: dist.ProcessGroup | None = None,
+                 decode_fn: DecodeFn | None = None, merge_fn: MergeFn | None = None):
+        if mode not in MODES:
+            raise ValueError(f"mode must be one of {MODES}")
+        self.mode = mode
+        self.group = group
+        self.decode_fn = decode_fn
+        self.merge_fn = merge_fn
+        self._send: torch.Tensor | None = None
+        self._recv: torch.Tensor | None = None
+
+    @property
+    def world(self) -> int:
+        return dist.get_world_size(self.group) if dist.is_initialized() else 1
+
+    @property
+    def rank(self) -> int:
+        return dist.get_rank(self.group) if dist.is_initialized() else 0
+
+    def _send_buffer(self, n: int, device: torch.device) -> torch.Tensor:
+        if self._send is None or self._send.numel() != n or self._send.device != device:
+            self._send = torch.empty(n, dtype=torch.float32, device=device)
+        return self._send
+
+    def _local(self, query: torch.Tensor, local: PackedBatch, sm_scale: float) -> torch.Tensor:
+        """Decodes ``query`` over ``local`` into the flat send row [out (QH*D) | lse (QH)]."""
+        qh, d = query.shape
+        send = self._send_buffer(qh * d + qh, query.device)
+        out_v, lse_v = send[: qh * d].view(qh, d), send[qh * d :]
+        if local.packed_k.shape[0] == 0:  # an empty shard: no weight in the merge
+            out_v.zero_()
+            lse_v.fill_(float("-inf"))
+        elif self.decode_fn is None:
+            from . import ops
+
+            PackedBatch.validate(local, query)
+            ops.decode(query, local.packed_k.contiguous(), local.packed_v.contiguous(),
+                       local.scales_k.contiguous(), local.scales_v.contiguous(),
+                       local.valid_tokens.to(torch.int32).contiguous(), local.bits,
+                       local.group_size, sm_scale, out=out_v, lse=lse_v)
+        else:
+            out, lse = self.decode_fn(query, local, sm_scale)
+            out_v.copy_(out)
+            lse_v.copy_(lse)
+        return send
+
+    def _gather(self, send: torch.Tensor) -> torch.Tensor:
+        world = self.world
+        n = send.numel()
+        if self._recv is None or self._recv.numel() != world * n or \
+                self._recv.device != send.device:
+            self._recv = torch.empty(world * n, dtype=send.dtype, device=send.device)
+        if world == 1:
+            self._recv.copy_(send)
+        else:
+            dist.all_gather_into_tensor(self._recv, send, group=self.group)
+        return self._recv.view(world, n)
+
+    def run(self, query: torch.Tensor, local: PackedBatch,
+            sm_scale: float) -> tuple[torch.Tensor, torch.Tensor]:
+        qh, d = query.shape
+        if self.mode == "heads":
+            kvh_local = local.packed_k.shape[2]
+            world = self.world
+            if kvh_local * world * (qh // (kvh_local * world)) != qh:
+                raise ValueError("query heads must be divisible by the sharded KV heads")
+            _, _, q_lo, q_hi = head_shard(kvh_local * world, qh, self.rank, world)
+            rows = q_hi - q_lo
+            recv = self._gather(self._local(query[q_lo:q_hi].contiguous(), local, sm_scale))
+            out_all = recv[:, : rows * d].reshape(world * rows, d)
+            lse_all = recv[:, rows * d :].reshape(world * rows)
+            return out_all.clone(), lse_all.clone()
+
+        recv = self._gather(self._local(query, local, sm_scale))
+        outs = recv[:, : qh * d].reshape(-1, qh, d).contiguous()
+        lses = recv[:, qh * d :].contiguous()
+        merge = self.merge_fn or _default_merge()
+        return merge(outs, lses)

@@ -1,6 +1,6 @@
 """Generates the golden fixtures in this directory from the reference implementation.
 
-Run in a container that has the reference checked out (default /root/reference):
+Run where the reference project is checked out (its path in --reference or $KVSSD_REFERENCE):
 
     python tests/golden/make_golden.py [--reference /path/to/kvssd-attention]
 
@@ -16,6 +16,7 @@ import argparse
 import hashlib
 import json
 import math
+import os
 import shutil
 import sys
 import tempfile
@@ -38,7 +39,7 @@ def u16(t: torch.Tensor) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("KVSSD_REFERENCE"), required="KVSSD_REFERENCE" not in os.environ)
     ap.add_argument("--skip-large", action="store_true", help="skip the full-size configs")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "src"))
