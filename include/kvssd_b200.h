@@ -94,6 +94,33 @@ KVSSD_B200_API int kvssd_b200_decode(const void* query, int query_dtype, const u
                       int group_size, float sm_scale, float* out, float* lse, void* workspace,
                       size_t workspace_bytes, kvssd_b200_stream_t stream);
 
+/* Bytes of the device scratch behind kvssd_b200_decode_static (one array per device). */
+#define KVSSD_B200_STATIC_SCRATCH_BYTES (8u << 20)
+
+/* kvssd_b200_decode without a caller workspace and without allocating anything: the split-KV
+ * parts and the status word live in a file-scope __device__ array of
+ * KVSSD_B200_STATIC_SCRATCH_BYTES per device. No counterpart in the reference (its op
+ * allocates its outputs with torch on every call, csrc/fused_decode.cu:125-127).
+ * For callers that cannot allocate device memory on the decode path: hosts that bind the C ABI
+ * without a device allocator of their own (a plain C, cgo or JNI host), and serving loops
+ * that must not call cudaMalloc/cudaFree there, which synchronise the device.
+ * Limits: a geometry whose plan needs more than KVSSD_B200_STATIC_SCRATCH_BYTES (256 bytes of
+ * header plus n_parts * query_heads * (head_dim + 2) * 4; the c2 shape needs 2.5 MB) is
+ * rejected with KVSSD_B200_ERR_WORKSPACE before anything is launched. The first call on each
+ * device resolves the scratch address and zeroes its 256-byte status header (the only part
+ * that must start at zero) on `stream`; make that first call before any stream capture.
+ * Every call on a device uses the same scratch, so calls on one device must not overlap in
+ * time (one stream, or events between streams): overlapping calls race on the parts.
+ * If `scratch` is not NULL it receives the scratch address, which kvssd_b200_read_status
+ * accepts as the workspace. Other arguments and outputs as kvssd_b200_decode. */
+KVSSD_B200_API int kvssd_b200_decode_static(const void* query, int query_dtype,
+                      const uint8_t* packed_k, const uint8_t* packed_v,
+                      const uint16_t* scales_k, const uint16_t* scales_v,
+                      const int32_t* valid_tokens, const int32_t* block_table,
+                      int n_pool_blocks, int n_sel_blocks, int block_tokens, int query_heads,
+                      int kv_heads, int head_dim, int bits, int group_size, float sm_scale,
+                      float* out, float* lse, void** scratch, kvssd_b200_stream_t stream);
+
 /* The two stages of kvssd_b200_decode, for callers that consume or exchange the split-KV
  * state themselves (e.g. timing the streaming kernel alone). decode_split takes the decode
  * arguments minus out/lse, runs the streaming kernel only and returns in *n_parts the number

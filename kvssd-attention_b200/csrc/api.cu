@@ -382,6 +382,76 @@ int kvssd_b200_decode(const void* query, int query_dtype, const uint8_t* packed_
   return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "combine launch");
 }
 
+}  // extern "C"
+
+namespace kvb {
+namespace {
+
+// Scratch of kvssd_b200_decode_static. A __device__ variable exists once per device context
+// that loads this module; no initializer, so nothing is embedded in the binary.
+__device__ __align__(256) unsigned char g_static_scratch[KVSSD_B200_STATIC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+// Address of the current device's scratch. The first call per device resolves the symbol
+// (with the device current) and zeroes the status header on `s`.
+int static_scratch(cudaStream_t s, void** ptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(KVSSD_B200_ERR_UNSUPPORTED, "static scratch supports device ordinals below 64");
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "static scratch address");
+    e = cudaMemsetAsync(p, 0, kHeaderBytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "static scratch status clear");
+    g_scratch_ptr[dev] = p;
+  }
+  *ptr = g_scratch_ptr[dev];
+  return KVSSD_B200_OK;
+}
+
+}  // namespace
+}  // namespace kvb
+
+extern "C" {
+
+int kvssd_b200_decode_static(const void* query, int query_dtype, const uint8_t* packed_k,
+                             const uint8_t* packed_v, const uint16_t* scales_k,
+                             const uint16_t* scales_v, const int32_t* valid_tokens,
+                             const int32_t* block_table, int n_pool_blocks, int n_sel_blocks,
+                             int block_tokens, int query_heads, int kv_heads, int head_dim,
+                             int bits, int group_size, float sm_scale, float* out, float* lse,
+                             void** scratch, kvssd_b200_stream_t stream) {
+  if (!out || !lse) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "tensor pointers must not be NULL");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  void* ws = nullptr;
+  int st = static_scratch(s, &ws);
+  if (st) return st;
+  if (scratch) *scratch = ws;
+  DecodeArgs a;
+  Plan p;
+  st = prepare_decode(query, query_dtype, packed_k, packed_v, scales_k, scales_v, valid_tokens,
+                      block_table, n_pool_blocks, n_sel_blocks, block_tokens, query_heads,
+                      kv_heads, head_dim, bits, group_size, sm_scale, ws,
+                      KVSSD_B200_STATIC_SCRATCH_BYTES, a, p);
+  if (st == KVSSD_B200_ERR_WORKSPACE)
+    return fail(st, "this geometry needs " + std::to_string(p.ws_bytes) +
+                        " bytes of scratch; the static scratch holds " +
+                        std::to_string(KVSSD_B200_STATIC_SCRATCH_BYTES) +
+                        " (use kvssd_b200_decode with a caller workspace)");
+  if (st) return st;
+  st = launch_split(a, p, s);
+  if (st) return st;
+  cudaError_t e = launch_combine(a.part_acc, a.part_ml, p.n_parts, query_heads, head_dim, out, lse, s);
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "combine launch");
+}
+
 int kvssd_b200_decode_split(const void* query, int query_dtype, const uint8_t* packed_k,
                             const uint8_t* packed_v, const uint16_t* scales_k,
                             const uint16_t* scales_v, const int32_t* valid_tokens,

@@ -50,6 +50,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _c_void, _c_size, _c_void,  # workspace, bytes, stream
         ],
     ),
+    "kvssd_b200_decode_static": (
+        _c_int,
+        [
+            _c_void, _c_int, _c_void, _c_void, _c_void, _c_void, _c_void, _c_void,
+            _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+            _c_float, _c_void, _c_void, ctypes.POINTER(_c_void), _c_void,
+        ],
+    ),
     "kvssd_b200_decode_split": (
         _c_int,
         [
