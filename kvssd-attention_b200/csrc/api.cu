@@ -22,7 +22,7 @@ namespace kvb {
 using DecodeKernel = void (*)(const DecodeArgs);
 DecodeKernel tc_decode_kernel_for(int bits, int d, int group);
 DecodeKernel simt_decode_kernel_for(int d);
-DecodeKernel async_decode_kernel_for(int bits, int d, int group);
+DecodeKernel async_decode_kernel_for(int bits, int d, int group, int kvh);
 int async_threads();
 int async_warps();
 int async_depth();
@@ -133,7 +133,7 @@ int choose_path(int d, int bits, int group) {
 // geometry does not qualify (INT4, head_dim 128, group 32 or 64, KV heads dividing the 16
 // warps, at most 8 query heads per KV head).
 bool plan_streaming(const Geometry& g, const DeviceInfo& info, Plan& p) {
-  p.kernel = async_decode_kernel_for(g.bits, g.d, g.group);
+  p.kernel = async_decode_kernel_for(g.bits, g.d, g.group, g.kvh);
   if (p.kernel == nullptr) return false;
   if (p.n_qsub != 1 || async_warps() % g.kvh) return false;
   p.smem = static_cast<size_t>(async_warps()) * async_depth() * async_stage_bytes(g.group);

@@ -5,11 +5,15 @@
 // Work: one CTA of 16 warps per SM owns a contiguous range of 16-token tiles of the selection
 // for ALL KV heads, so the CTA's warps together read contiguous runs of token rows (kvssd's
 // record layout interleaves the KV heads of a token, src/kvssd/format.py:165). Warp w serves
-// KV head w % kv_heads and takes every wph-th tile of the range (wph = 16 / kv_heads).
+// KV head w % kv_heads and takes every wph-th tile of the range (wph = 16 / kv_heads); the
+// number of KV heads is a template parameter, so strides and the head mapping are constants.
 //
 // Feed: each warp copies, for its tiles only, the 16 K rows and 16 V rows of its head (64
 // bytes per row, 16-byte cp.async.cg, four lanes per row) and the rows' FP16 scales (8- or
-// 4-byte cp.async.ca) into a private ring of `depth` stages, depth-1 tiles ahead of its math.
+// 4-byte cp.async.ca) into a private ring of `depth` stages: a stage is refilled with the tile
+// `depth` ahead as soon as its data has moved to registers.
+// Inside a block the copy addresses advance by constant strides and the block table is read
+// once per block; tiles with fewer than 16 valid rows are flagged per stage.
 // Warps wait only for their own copies (cp.async.wait_group + __syncwarp), never for each
 // other, so the 16 warps drift apart and the scheduler interleaves one warp's copies and
 // shuffles with another's tensor-core work, while ~160 KB per SM stays in flight without
@@ -18,12 +22,9 @@
 //
 // Math (per warp, per tile of 16 tokens): with 32 dims per 16-byte chunk and group_size >= 32,
 // every k-step of QK and every M-tile of PV lies inside one scale group, so scales are applied
-// outside the tensor-core products:
-//   QK: S[t,n] = sum_group sk[t,group] * (sum_{d in group} (code-mid)[t,d] * q[n,d]);
-//       the codes enter the mma as the raw FP16 values 1024+n / 1024+16n (q pre-divided by 16
-//       for the latter); each group's FP32 accumulator starts at -C, C being the constant those
-//       encodings add (computed once by the same mma from constant rows), so it ends at the
-//       exact centred product; one FFMA per element then applies the K scale;
+// outside the tensor-core products, which multiply exact centred codes:
+//   QK: S[t,n] = sum_group sk[t,group] * (sum_{d in group} (code-mid)[t,d] * q[n,d])
+//       -- two m16n8k16 per group into a fresh FP32 accumulator, then one FFMA per element;
 //   PV: O^T[d,n] = sum_t (code-mid)[t,d] * (P[t,n] * sv[t,group(d)])
 //       -- the V scale is folded into the FP16 P operand of the M-tiles of that group;
 //   ldmatrix.trans delivers V with two tokens per 32-bit register, the pairing the PV A
@@ -54,104 +55,148 @@ struct ScaleRow {  // the G FP16 scales of one (token, KV head)
   }
 };
 
-// Raw K codes for the QK mma: (1024 + n) in the even and (1024 + 16n) in the odd code slots of
-// each 16-bit lane, two instructions fewer per pair than centring; the constant offsets are
-// cancelled exactly through the accumulator start value (see async_decode_kernel).
-__device__ __forceinline__ void magic_pairs(uint32_t x, uint32_t (&o)[4]) {
-  const uint32_t x8 = x >> 8;
-  o[0] = or_magic<0x000F000Fu>(x);
-  o[1] = or_magic<0x00F000F0u>(x);
-  o[2] = or_magic<0x000F000Fu>(x8);
-  o[3] = or_magic<0x00F000F0u>(x8);
-}
-
-// D = A * B with a zero accumulator start (no register moves for C).
-__device__ __forceinline__ void mma_16816_set(float (&d)[4], uint32_t a0, uint32_t a1,
-                                              uint32_t a2, uint32_t a3, uint32_t b0,
-                                              uint32_t b1, float c0, float c1) {
+// D = A * B (zero accumulator start).
+__device__ __forceinline__ void mma_16816_zero(float (&d)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
   asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};\n"
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
 }
 
-template <int GROUP>
+// Copy side of one warp: the addresses of its next tile and the cursor over the selection.
+// Consecutive tiles of a warp inside one block are 16 * WPH rows apart, so inside a block the
+// lane addresses advance by constant strides; the block table is consulted once per block.
+// Lane (r, q) copies 16-byte chunk q of rows r and r + 8 of K and V (chunk q of row r stored at
+// chunk q ^ ((r >> 1) & 3)); lanes 0-15 copy K scale row (lane & 15), lanes 16-31 the V one.
+template <int KVH, int G>
+struct WarpFeed {
+  static constexpr int PD = 64, SB = 2 * G, WPH = kAsyncWarps / KVH;
+  static constexpr int ROW = KVH * PD, SROW = KVH * SB;  // bytes per token row
+  static constexpr int STEP = 16 * WPH;                  // rows between this warp's tiles
+  const uint8_t* gk;  // this lane's K / V / scale source for the next tile
+  const uint8_t* gv;
+  const uint8_t* gs;
+  int slot, tib;  // cursor: selection slot and tile-in-block of the next block's first tile
+  int off;        // row offset of the next tile in its block (>= block_tokens: block done)
+  int valid = 0;  // valid rows of the current block (0 for a refused block-table entry)
+
+  // Moves to the block that holds the next tile: one (cached) block-table lookup.
+  __device__ __forceinline__ void enter_block(const DecodeArgs& a, BlockInfoCache& cache,
+                                              int lane, int h) {
+    const int tpb = a.tiles_per_block;
+    while (tib >= tpb) {
+      tib -= tpb;
+      ++slot;
+    }
+    int blk;
+    cache.lookup(a, slot, lane, blk, valid);
+    if (blk < 0) {
+      blk = 0;
+      valid = 0;
+    }
+    off = tib * 16;
+    tib += (tpb - tib + WPH - 1) / WPH * WPH;  // past this warp's tiles of the block
+    const size_t row0 = static_cast<size_t>(blk) * a.bt + off;
+    const int cr = lane >> 2, cq = lane & 3, sr = lane & 15;
+    gk = a.kp + (row0 + cr) * ROW + h * PD + cq * 16;
+    gv = a.vp + (row0 + cr) * ROW + h * PD + cq * 16;
+    gs = reinterpret_cast<const uint8_t*>(lane < 16 ? a.ks : a.vs) + (row0 + sr) * SROW + h * SB;
+  }
+
+  __device__ __forceinline__ void advance() {
+    gk += STEP * ROW;
+    gv += STEP * ROW;
+    gs += STEP * SROW;
+    off += STEP;
+  }
+};
+
+template <int KVH, int GROUP>
 __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const DecodeArgs a) {
   constexpr int D = 128, BITS = 4, G = D / GROUP, MT = D / 16, DEPTH = kAsyncDepth;
   constexpr int PD = D * BITS / 8;            // 64 bytes of codes per (token, head)
   constexpr int SB = 2 * G;                   // scale bytes per (token, head)
   constexpr int OFF_V = 16 * PD, OFF_KS = 32 * PD, OFF_VS = OFF_KS + 16 * SB;
   constexpr int STAGE = ((OFF_VS + 16 * SB) + 127) / 128 * 128;
+  constexpr int WPH = kAsyncWarps / KVH;
   constexpr float kLazyMax = 8.f;  // rescale only when a score beats the running max by 2^8
+  using Feed = WarpFeed<KVH, G>;
   static_assert(G == 4 || G == 2, "scale rows must be whole 4-byte words");
+  static_assert(DEPTH <= 32, "partial-tile flags are one bit per stage");
   extern __shared__ __align__(128) uint8_t smem[];
   asm volatile("griddepcontrol.launch_dependents;");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, c = lane & 3;
-  const int kvh = a.kvh, wph = a.wph;
-  const int h = warp % kvh, sub = warp / kvh;
+  const int h = warp % KVH, sub = warp / KVH;
   uint8_t* ring = smem + static_cast<size_t>(warp) * DEPTH * STAGE;
   const uint32_t ring_s = smem_addr(ring);
-  __shared__ int tile_rows[kAsyncWarps][DEPTH];
+  __shared__ int tile_rows[kAsyncWarps][DEPTH];  // valid rows of stages flagged partial
 
   const long long t_begin = a.total_tiles * blockIdx.x / a.n_splits;
   const int n_tiles = static_cast<int>(a.total_tiles * (blockIdx.x + 1) / a.n_splits - t_begin);
-  const int n_mine = sub < n_tiles ? (n_tiles - sub + wph - 1) / wph : 0;
+  const int n_mine = sub < n_tiles ? (n_tiles - sub + WPH - 1) / WPH : 0;
 
   // ---------------- feed: this warp's copies of its i-th tile into stage i % DEPTH
-  // Lane (r, q) copies 16-byte chunk q of rows r and r+8 of K and V (chunk q of row r is stored
-  // at chunk q ^ ((r >> 1) & 3)); lanes 0-15 copy the K scale row, lanes 16-31 the V scale row.
-  const int row_bytes = kvh * PD;
-  const int srow = kvh * SB;
-  const int cr = lane >> 2, cq = lane & 3, sr = lane & 15;
-  const uint32_t dst_kv = cr * PD + ((cq ^ ((cr >> 1) & 3)) << 4);
+  const int cr = lane >> 2, sr = lane & 15;
+  const uint32_t dst_kv =
+      static_cast<uint32_t>(cr * PD + (((lane & 3) ^ ((cr >> 1) & 3)) << 4));
   const uint32_t dst_s = (lane < 16 ? OFF_KS : OFF_VS) + sr * SB;
-  const uint8_t* k_lane = a.kp + h * PD + cr * row_bytes + cq * 16;
-  const uint8_t* v_lane = a.vp + h * PD + cr * row_bytes + cq * 16;
-  const uint8_t* s_lane = reinterpret_cast<const uint8_t*>(lane < 16 ? a.ks : a.vs) + h * SB +
-                          sr * srow;
   const uint64_t policy = l2_evict_first();
   BlockInfoCache cache;
-  TileCursor cur;
-  cur.seek(t_begin + sub, a.tiles_per_block);
-  int fill_slot = 0;
-  auto issue = [&](int i) {
-    if (i < n_mine) {
-      const int off = cur.row_offset();
-      int blk, valid;
-      cache.lookup(a, cur.slot, lane, blk, valid);
-      cur.advance(wph, a.tiles_per_block);
-      const int rows = blk >= 0 ? max(0, min(valid - off, 16)) : 0;
-      if (lane == 0) tile_rows[warp][fill_slot] = rows;
-      if (rows > 0) {
-        const size_t row0 = static_cast<size_t>(blk) * a.bt + off;
-        const size_t kv_off = row0 * row_bytes, s_off = row0 * srow;
-        const uint32_t st = ring_s + fill_slot * STAGE;
-        if (cr < rows) {
-          cp_async16(st + dst_kv, k_lane + kv_off, policy);
-          cp_async16(st + OFF_V + dst_kv, v_lane + kv_off, policy);
+  Feed feed;
+  {
+    const long long t = t_begin + sub;
+    feed.slot = static_cast<int>(t / a.tiles_per_block);
+    feed.tib = static_cast<int>(t - static_cast<long long>(feed.slot) * a.tiles_per_block);
+  }
+  uint32_t partial = 0;  // bit s: stage s holds a tile with fewer than 16 valid rows
+  // Copies tile `tile` of this warp into stage `fill_slot` (shared address fill_st).
+  auto issue = [&](int tile, int fill_slot, uint32_t fill_st) {
+    if (tile < n_mine) {
+      if (tile == 0 || feed.off >= a.bt) feed.enter_block(a, cache, lane, h);
+      const int rows = feed.valid - feed.off;
+      if (rows >= 16) {
+        cp_async16(fill_st + dst_kv, feed.gk, policy);
+        cp_async16(fill_st + OFF_V + dst_kv, feed.gv, policy);
+        cp_async16(fill_st + 8 * PD + dst_kv, feed.gk + 8 * Feed::ROW, policy);
+        cp_async16(fill_st + OFF_V + 8 * PD + dst_kv, feed.gv + 8 * Feed::ROW, policy);
+        if constexpr (G == 4) cp_async8(fill_st + dst_s, feed.gs, policy);
+        else cp_async4(fill_st + dst_s, feed.gs, policy);
+        partial &= ~(1u << fill_slot);
+      } else {
+        // Ragged tail: rows past the valid count are not copied (their scores are masked);
+        // their scale rows repeat the last valid row so every scale in the stage is finite.
+        const int rc = max(rows, 0);
+        if (cr < rc) {
+          cp_async16(fill_st + dst_kv, feed.gk, policy);
+          cp_async16(fill_st + OFF_V + dst_kv, feed.gv, policy);
         }
-        if (cr + 8 < rows) {
-          cp_async16(st + 8 * PD + dst_kv, k_lane + kv_off + 8 * row_bytes, policy);
-          cp_async16(st + OFF_V + 8 * PD + dst_kv, v_lane + kv_off + 8 * row_bytes, policy);
+        if (cr + 8 < rc) {
+          cp_async16(fill_st + 8 * PD + dst_kv, feed.gk + 8 * Feed::ROW, policy);
+          cp_async16(fill_st + OFF_V + 8 * PD + dst_kv, feed.gv + 8 * Feed::ROW, policy);
         }
-        if (sr < rows) {
-          if constexpr (G == 4) cp_async8(st + dst_s, s_lane + s_off, policy);
-          else cp_async4(st + dst_s, s_lane + s_off, policy);
+        if (rc > 0) {
+          const uint8_t* src = feed.gs + (min(sr, rc - 1) - sr) * Feed::SROW;
+          if constexpr (G == 4) cp_async8(fill_st + dst_s, src, policy);
+          else cp_async4(fill_st + dst_s, src, policy);
         }
+        if (lane == 0) tile_rows[warp][fill_slot] = rc;
+        partial |= 1u << fill_slot;
       }
-      if (++fill_slot == DEPTH) fill_slot = 0;
+      feed.advance();
     }
     cp_async_commit();
   };
 #pragma unroll 1
-  for (int i = 0; i < DEPTH - 1; ++i) issue(i);
+  for (int i = 0; i < DEPTH; ++i) issue(i, i, ring_s + i * STAGE);
 
   // ---------------- compute state
   const int q0 = h * a.gqa, nq = a.gqa;
   // Q (pre-multiplied by sm_scale*log2(e)) as the B operand: k-step (m, j2) of thread c covers
   // dims 32m + 8c + {2j2, 2j2+4} (b0, even code slots) and 32m + 8c + {2j2+1, 2j2+5} (b1, odd
-  // code slots, divided by 16 to match the (1024 + 16n) encoding; exact power-of-two scaling).
+  // code slots), the order in which the unpacker emits a 32-bit word's codes.
   uint32_t qf[4][2][2];
 #pragma unroll
   for (int m = 0; m < 4; ++m)
@@ -163,25 +208,11 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
         float f0 = 0.f, f1 = 0.f;
         if (g < nq) {
           const long long qb = static_cast<long long>(q0 + g) * D;
-          const float sc = r ? a.score_scale * 0.0625f : a.score_scale;
-          f0 = load_query(a.q, a.q_dtype, qb + d0) * sc;
-          f1 = load_query(a.q, a.q_dtype, qb + d1) * sc;
+          f0 = load_query(a.q, a.q_dtype, qb + d0) * a.score_scale;
+          f1 = load_query(a.q, a.q_dtype, qb + d1) * a.score_scale;
         }
         qf[m][j2][r] = h2_as_u32(__floats2half2_rn(f0, f1));
       }
-  // Per group m and head column: the constant the raw encoding adds to the QK product,
-  // C = sum_even 1032 q + sum_odd 1152 q/16 -- computed with the same mma from constant A rows,
-  // so each group's accumulator starts at -C and ends at sum (code - 8) q exactly.
-  float cneg[4][2];
-#pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    float c4[4];
-    mma_16816_set(c4, 0x64086408u, 0x64086408u, 0x64806480u, 0x64806480u, qf[m][0][0],
-                  qf[m][0][1], 0.f, 0.f);
-    mma_16816(c4, 0x64086408u, 0x64086408u, 0x64806480u, 0x64806480u, qf[m][1][0], qf[m][1][1]);
-    cneg[m][0] = -c4[0];
-    cneg[m][1] = -c4[1];
-  }
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   float acc[MT][4];
 #pragma unroll
@@ -194,55 +225,48 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
   const uint32_t sk_off = OFF_KS + g * SB, sv_off = OFF_VS + 2 * c * SB;
 
   int slot = 0;
+  uint32_t st = ring_s;  // shared address of the stage consumed next
 #pragma unroll 1
   for (int i = 0; i < n_mine; ++i) {
-    cp_async_wait<DEPTH - 2>();  // this lane's copies of tile i have landed
+    cp_async_wait<DEPTH - 1>();  // this lane's copies of tile i have landed
     __syncwarp();                // ... and every lane's
-    const int rows = tile_rows[warp][slot];
-    const uint32_t st = ring_s + slot * STAGE;
-    const uint8_t* sp = ring + slot * STAGE;
+    int rows = 16;
+    if (partial & (1u << slot)) rows = tile_rows[warp][slot];
+    const uint8_t* sp = ring + (st - ring_s);
     uint32_t kA[4], kB[4], vA[4], vB[4];
     ScaleRow<G> sk0, sk1, sv[4];
-    if (rows == 16) {
-      ldsm_x4(st + ld_off, kA[0], kA[1], kA[2], kA[3]);               // K tokens 0-7
-      ldsm_x4(st + ld_off + 8 * PD, kB[0], kB[1], kB[2], kB[3]);      // K tokens 8-15
-      ldsm_x4_trans(st + OFF_V + ld_off, vA[0], vA[1], vA[2], vA[3]);
-      ldsm_x4_trans(st + OFF_V + ld_off + 8 * PD, vB[0], vB[1], vB[2], vB[3]);
-      sk0.load(sp + sk_off);
-      sk1.load(sp + sk_off + 8 * SB);
-      sv[0].load(sp + sv_off);
-      sv[1].load(sp + sv_off + SB);
-      sv[2].load(sp + sv_off + 8 * SB);
-      sv[3].load(sp + sv_off + 9 * SB);
-    } else if (rows > 0) {  // partial tile: rows past the valid count re-read the last one
-      ldsm_x4(st + ld_off, kA[0], kA[1], kA[2], kA[3]);
-      ldsm_x4(st + ld_off + 8 * PD, kB[0], kB[1], kB[2], kB[3]);
-      ldsm_x4_trans(st + OFF_V + ld_off, vA[0], vA[1], vA[2], vA[3]);
-      ldsm_x4_trans(st + OFF_V + ld_off + 8 * PD, vB[0], vB[1], vB[2], vB[3]);
-      const int last = rows - 1;
-      sk0.load(sp + OFF_KS + min(g, last) * SB);
-      sk1.load(sp + OFF_KS + min(g + 8, last) * SB);
-      sv[0].load(sp + OFF_VS + min(2 * c, last) * SB);
-      sv[1].load(sp + OFF_VS + min(2 * c + 1, last) * SB);
-      sv[2].load(sp + OFF_VS + min(2 * c + 8, last) * SB);
-      sv[3].load(sp + OFF_VS + min(2 * c + 9, last) * SB);
+    ldsm_x4(st + ld_off, kA[0], kA[1], kA[2], kA[3]);               // K tokens 0-7
+    ldsm_x4(st + ld_off + 8 * PD, kB[0], kB[1], kB[2], kB[3]);      // K tokens 8-15
+    ldsm_x4_trans(st + OFF_V + ld_off, vA[0], vA[1], vA[2], vA[3]);
+    ldsm_x4_trans(st + OFF_V + ld_off + 8 * PD, vB[0], vB[1], vB[2], vB[3]);
+    sk0.load(sp + sk_off);
+    sk1.load(sp + sk_off + 8 * SB);
+    sv[0].load(sp + sv_off);
+    sv[1].load(sp + sv_off + SB);
+    sv[2].load(sp + sv_off + 8 * SB);
+    sv[3].load(sp + sv_off + 9 * SB);
+    __syncwarp();                   // the stage's data is in registers: refill it
+    issue(i + DEPTH, slot, st);     // with the tile DEPTH ahead
+    if (++slot == DEPTH) {
+      slot = 0;
+      st = ring_s;
+    } else {
+      st += STAGE;
     }
-    __syncwarp();         // the slot's data is in registers: it may be refilled
-    issue(i + DEPTH - 1);  // into the slot consumed one iteration ago
-    if (++slot == DEPTH) slot = 0;
     if (rows <= 0) continue;
 
     // ---- QK per scale group: r4 = sum_group (code - 8) q, then scaled by the K scale
     float x[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
-      uint32_t p0[4], p1[4];
-      magic_pairs(kA[m], p0);
-      magic_pairs(kB[m], p1);
+      __half2 p0[4], p1[4];
+      LanePairs<BITS>::centred(kA[m], p0);
+      LanePairs<BITS>::centred(kB[m], p1);
       float r4[4];
-      mma_16816_set(r4, p0[0], p1[0], p0[1], p1[1], qf[m][0][0], qf[m][0][1], cneg[m][0],
-                    cneg[m][1]);
-      mma_16816(r4, p0[2], p1[2], p0[3], p1[3], qf[m][1][0], qf[m][1][1]);
+      mma_16816_zero(r4, h2_as_u32(p0[0]), h2_as_u32(p1[0]), h2_as_u32(p0[1]), h2_as_u32(p1[1]),
+                     qf[m][0][0], qf[m][0][1]);
+      mma_16816(r4, h2_as_u32(p0[2]), h2_as_u32(p1[2]), h2_as_u32(p0[3]), h2_as_u32(p1[3]),
+                qf[m][1][0], qf[m][1][1]);
       const int gi = (32 * m) / GROUP;
       const float s0 = __half2float(sk0.s[gi]), s1 = __half2float(sk1.s[gi]);
       x[0] = fmaf(r4[0], s0, x[0]);
@@ -251,7 +275,7 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
       x[3] = fmaf(r4[3], s1, x[3]);
     }
     // ---- online softmax in the log2 domain; rows g, g+8 x heads 2c, 2c+1
-    if (rows < 16) {
+    if (rows < 16) {  // rows past the valid count hold stale codes: no weight
       if (g >= rows) x[0] = x[1] = -INFINITY;
       if (g + 8 >= rows) x[2] = x[3] = -INFINITY;
     }
@@ -308,7 +332,7 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
   constexpr int kFields = 4 + 4 * MT;
   float* buf = reinterpret_cast<float*>(smem);
   if (sub > 0) {
-    float* dst = buf + static_cast<size_t>((sub - 1) * kvh + h) * kFields * 32 + lane;
+    float* dst = buf + static_cast<size_t>((sub - 1) * KVH + h) * kFields * 32 + lane;
     dst[0] = m_run[0];
     dst[32] = m_run[1];
     dst[64] = l_run[0];
@@ -320,8 +344,8 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
   }
   __syncthreads();
   if (sub > 0) return;
-  for (int o = 1; o < wph; ++o) {
-    const float* src = buf + static_cast<size_t>((o - 1) * kvh + h) * kFields * 32 + lane;
+  for (int o = 1; o < WPH; ++o) {
+    const float* src = buf + static_cast<size_t>((o - 1) * KVH + h) * kFields * 32 + lane;
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       const float mo = src[hh * 32], lo = src[(2 + hh) * 32];
@@ -365,12 +389,24 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
 using DecodeKernel = void (*)(const DecodeArgs);
 
 // INT4, head_dim 128, group_size 32 or 64 (16-byte code chunks inside one scale group; scale
-// rows of whole 4-byte words).
-DecodeKernel async_decode_kernel_for(int bits, int d, int group) {
+// rows of whole 4-byte words), KV heads dividing the 16 warps of a CTA.
+template <int GROUP>
+DecodeKernel async_kernel_for_heads(int kvh) {
+  switch (kvh) {
+    case 1: return async_decode_kernel<1, GROUP>;
+    case 2: return async_decode_kernel<2, GROUP>;
+    case 4: return async_decode_kernel<4, GROUP>;
+    case 8: return async_decode_kernel<8, GROUP>;
+    case 16: return async_decode_kernel<16, GROUP>;
+    default: return nullptr;
+  }
+}
+
+DecodeKernel async_decode_kernel_for(int bits, int d, int group, int kvh) {
   if (bits != 4 || d != 128) return nullptr;
   switch (group) {
-    case 32: return async_decode_kernel<32>;
-    case 64: return async_decode_kernel<64>;
+    case 32: return async_kernel_for_heads<32>(kvh);
+    case 64: return async_kernel_for_heads<64>(kvh);
     default: return nullptr;
   }
 }
