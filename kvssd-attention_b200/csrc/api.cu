@@ -52,7 +52,7 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 constexpr size_t kHeaderBytes = 256;  // workspace header: device status word + padding
-constexpr int kMaxParts = 8192;       // bound on split-KV parts (combine shared memory)
+constexpr int kMaxParts = 8192;       // bound on split-KV parts
 
 struct DeviceInfo {
   int sms = 0;
@@ -199,7 +199,7 @@ cudaError_t launch_combine(const float* part_acc, const float* part_ml, int n_pa
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(qh, (d + 31) / 32, 1);
   cfg.blockDim = dim3(kCombineThreads, 1, 1);
-  cfg.dynamicSmemBytes = static_cast<size_t>(n_parts) * sizeof(float);
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -15,10 +15,12 @@
 // Inside a block the copy addresses advance by constant strides and the block table is read
 // once per block; tiles with fewer than 16 valid rows are flagged per stage.
 // Warps wait only for their own copies (cp.async.wait_group + __syncwarp), never for each
-// other, so the 16 warps drift apart and the scheduler interleaves one warp's copies and
-// shuffles with another's tensor-core work, while ~160 KB per SM stays in flight without
-// occupying registers. Rows are stored with chunk q of row r at chunk q ^ ((r >> 1) & 3), so
-// the 8 rows an ldmatrix reads fall on 8 distinct bank groups.
+// other, so the 16 warps drift apart and the scheduler interleaves one warp's copies with
+// another's tensor-core work. Two stages per warp (74 KB per SM, ~11 MB in flight over the
+// GPU, above HBM's bandwidth-latency product) measured fastest: deeper rings (3..6 stages)
+// were 1-5 % slower, and the small ring leaves most of the SM's L1 to the 8-byte scale copies,
+// whose 32-byte sectors are shared by four KV heads. Rows are stored with chunk q of row r at
+// chunk q ^ ((r >> 1) & 3), so the 8 rows an ldmatrix reads fall on 8 distinct bank groups.
 //
 // Math (per warp, per tile of 16 tokens): with 32 dims per 16-byte chunk and group_size >= 32,
 // every k-step of QK and every M-tile of PV lies inside one scale group, so scales are applied
@@ -39,7 +41,7 @@ namespace kvb {
 
 constexpr int kAsyncWarps = 16;
 constexpr int kAsyncThreads = 32 * kAsyncWarps;
-constexpr int kAsyncDepth = 6;  // ring stages per warp (compile-time: cp.async.wait_group N)
+constexpr int kAsyncDepth = 2;  // ring stages per warp (compile-time: cp.async.wait_group N)
 
 template <int G>
 struct ScaleRow {  // the G FP16 scales of one (token, KV head)
