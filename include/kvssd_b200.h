@@ -42,7 +42,7 @@ enum kvssd_b200_status {
   KVSSD_B200_ERR_UNSUPPORTED = 2,      /* valid kvssd input outside this library's range */
   KVSSD_B200_ERR_WORKSPACE = 3,        /* workspace missing or smaller than required */
   KVSSD_B200_ERR_CUDA = 4,             /* a CUDA runtime call or launch failed */
-  KVSSD_B200_ERR_DEVICE_STATUS = 5     /* kernels flagged bad block-table/valid entries */
+  KVSSD_B200_ERR_DEVICE_STATUS = 5     /* kernels flagged bad table/valid entries or a timeout */
 };
 
 enum kvssd_b200_query_dtype {
@@ -83,9 +83,11 @@ KVSSD_B200_API int kvssd_b200_decode_workspace_size(int n_sel_blocks, int block_
  * (bindings.cpp:26-38, fused_decode.cu:117-121) plus the block table. Invalid block-table or
  * valid_tokens entries are never dereferenced: they are skipped/clamped and recorded in the
  * workspace status word (see kvssd_b200_read_status). Outputs: out, lse as in the header.
- * The workspace (>= kvssd_b200_decode_workspace_size bytes, 16-byte aligned) starts with that
- * sticky status word: zero its first 256 bytes once after allocating it. Calls sharing one
- * workspace must be ordered on the GPU (same stream or explicit events). */
+ * The workspace (>= kvssd_b200_decode_workspace_size bytes, 16-byte aligned) starts with a
+ * 256-byte header holding that sticky status word and the arrival counters of the fused
+ * combine (the streaming kernel folds its split-KV parts itself; the counters return to zero
+ * at the end of every call): zero the header once after allocating the workspace. Calls
+ * sharing one workspace must be ordered on the GPU (same stream or explicit events). */
 KVSSD_B200_API int kvssd_b200_decode(const void* query, int query_dtype, const uint8_t* packed_k,
                       const uint8_t* packed_v, const uint16_t* scales_k,
                       const uint16_t* scales_v, const int32_t* valid_tokens,
@@ -153,7 +155,8 @@ KVSSD_B200_API int kvssd_b200_set_path_override(int path);
 
 /* Reads (synchronising `stream`) and optionally clears the device status word of a decode
  * workspace; *device_status receives the OR of flagged conditions (1 = block-table entry out
- * of range, 2 = valid_tokens entry out of [0, block_tokens]). Returns
+ * of range, 2 = valid_tokens entry out of [0, block_tokens], 4 = a fused combine gave up after
+ * waiting about a second for the other CTAs' parts; out/lse of that call are invalid). Returns
  * KVSSD_B200_ERR_DEVICE_STATUS when it is nonzero. No reference counterpart. */
 KVSSD_B200_API int kvssd_b200_read_status(void* workspace, int clear, unsigned* device_status,
                            kvssd_b200_stream_t stream);

@@ -51,7 +51,8 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(KVSSD_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-constexpr size_t kHeaderBytes = 256;  // workspace header: device status word + padding
+constexpr size_t kHeaderBytes = 256;  // workspace header: device status word, counters, padding
+constexpr size_t kTicketOffset = 128;  // the fused combine's two arrival counters
 constexpr int kMaxParts = 8192;       // bound on split-KV parts
 
 struct DeviceInfo {
@@ -226,7 +227,8 @@ const char* kvssd_b200_status_string(int status) {
     case KVSSD_B200_ERR_UNSUPPORTED: return "unsupported";
     case KVSSD_B200_ERR_WORKSPACE: return "workspace too small";
     case KVSSD_B200_ERR_CUDA: return "CUDA error";
-    case KVSSD_B200_ERR_DEVICE_STATUS: return "device flagged invalid block-table or valid_tokens entries";
+    case KVSSD_B200_ERR_DEVICE_STATUS:
+      return "device flagged invalid block-table or valid_tokens entries, or a combine timeout";
     default: return "unknown status";
   }
 }
@@ -339,19 +341,66 @@ int prepare_decode(const void* query, int query_dtype, const uint8_t* packed_k,
   a.score_scale = sm_scale * 1.4426950408889634f;  // log2(e): scores kept in log2 units
   char* ws = static_cast<char*>(workspace);
   a.status = reinterpret_cast<unsigned*>(ws);
+  a.tickets = reinterpret_cast<unsigned*>(ws + kTicketOffset);
+  a.fuse_combine = 0;
+  a.out = nullptr;
+  a.lse = nullptr;
   a.part_ml = reinterpret_cast<float*>(ws + kHeaderBytes);
   a.part_acc = a.part_ml + static_cast<size_t>(p.n_parts) * query_heads * 2;
   return KVSSD_B200_OK;
 }
 
-int launch_split(const DecodeArgs& a, const Plan& p, cudaStream_t s) {
+int launch_split(DecodeArgs& a, const Plan& p, cudaStream_t s);
+
+// The whole decode: the streaming kernel folds its parts itself (fused combine, cooperative
+// launch); the other kernels, or a refused cooperative launch, are followed by the combine
+// kernel.
+int launch_decode(DecodeArgs& a, const Plan& p, float* out, float* lse, cudaStream_t s) {
+  if (p.streaming) {
+    a.fuse_combine = 1;
+    a.out = out;
+    a.lse = lse;
+    const int st = launch_split(a, p, s);
+    if (st == KVSSD_B200_OK || a.fuse_combine) return st;
+    // cooperative launch refused (a.fuse_combine cleared): two-launch path below
+  }
+  int st = launch_split(a, p, s);
+  if (st) return st;
+  cudaError_t e = launch_combine(a.part_acc, a.part_ml, p.n_parts, a.qh, a.d, out, lse, s);
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "combine launch");
+}
+
+int launch_split(DecodeArgs& a, const Plan& p, cudaStream_t s) {
   if (p.smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(p.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(p.smem));
     if (e != cudaSuccess) return cuda_fail(e, "shared-memory attribute");
   }
-  p.kernel<<<dim3(p.n_splits, p.n_head_groups, 1), dim3(p.threads, 1, 1), p.smem, s>>>(a);
-  cudaError_t e = cudaGetLastError();
+  if (!p.streaming) {
+    p.kernel<<<dim3(p.n_splits, p.n_head_groups, 1), dim3(p.threads, 1, 1), p.smem, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "decode launch");
+  }
+  // Streaming kernel: programmatic stream serialization (it waits for the preceding grid
+  // itself) and, with the fused combine, a cooperative launch so its CTAs are co-resident.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.n_splits, p.n_head_groups, 1);
+  cfg.blockDim = dim3(p.threads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.fuse_combine ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, p.kernel, a);
+  if (e == cudaErrorCooperativeLaunchTooLarge && a.fuse_combine) {
+    cudaGetLastError();  // not sticky: fall back to the two-launch decode
+    a.fuse_combine = 0;
+    return KVSSD_B200_ERR_UNSUPPORTED;
+  }
   return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "decode launch");
 }
 
@@ -375,11 +424,7 @@ int kvssd_b200_decode(const void* query, int query_dtype, const uint8_t* packed_
                           kv_heads, head_dim, bits, group_size, sm_scale, workspace,
                           workspace_bytes, a, p);
   if (st) return st;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  st = launch_split(a, p, s);
-  if (st) return st;
-  cudaError_t e = launch_combine(a.part_acc, a.part_ml, p.n_parts, query_heads, head_dim, out, lse, s);
-  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "combine launch");
+  return launch_decode(a, p, out, lse, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
@@ -446,10 +491,7 @@ int kvssd_b200_decode_static(const void* query, int query_dtype, const uint8_t* 
                         std::to_string(KVSSD_B200_STATIC_SCRATCH_BYTES) +
                         " (use kvssd_b200_decode with a caller workspace)");
   if (st) return st;
-  st = launch_split(a, p, s);
-  if (st) return st;
-  cudaError_t e = launch_combine(a.part_acc, a.part_ml, p.n_parts, query_heads, head_dim, out, lse, s);
-  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "combine launch");
+  return launch_decode(a, p, out, lse, s);
 }
 
 int kvssd_b200_decode_split(const void* query, int query_dtype, const uint8_t* packed_k,

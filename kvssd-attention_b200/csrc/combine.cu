@@ -10,11 +10,10 @@
 //   (L = logaddexp(La, Lb); O = Oa*exp(La-L) + Ob*exp(Lb-L)).
 #include <cmath>
 
+#include "combine.cuh"
 #include "common.cuh"
 
 namespace kvb {
-
-constexpr float kLn2 = 0.693147180559945309f;
 
 __device__ __forceinline__ float block_reduce_max(float v, float* red) {
 #pragma unroll
@@ -42,76 +41,13 @@ __device__ __forceinline__ float block_reduce_sum(float v, float* red) {
   return v;
 }
 
-// grid = (query_heads, ceil(d / 32)), block = 32 * kCombineWarps threads. Warp w folds the
-// contiguous part range [w*n/W, (w+1)*n/W) for the 32 dims of its CTA, 32 parts per batch: all
-// of a batch's loads (lane j: part j's m and l; every lane: its dim of the 32 parts' rows) are
-// issued before any of them is used, so a batch costs one round trip to L2. Part weights reach
-// the other lanes by shuffle; the W warp states are merged through shared memory.
-constexpr int kCombineWarps = 16;
-
+// grid = (query_heads, ceil(d / 32)), block = 32 * kCombineWarps threads: one slice per CTA.
 __global__ void __launch_bounds__(32 * kCombineWarps) combine_parts_kernel(
     const float* __restrict__ part_acc, const float* __restrict__ part_ml, int n_parts, int qh,
     int d, float* __restrict__ out, float* __restrict__ lse) {
   // Parts are produced by the preceding decode grid (programmatic dependent launch).
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  __shared__ float wm[kCombineWarps], wl[kCombineWarps], wacc[kCombineWarps][32];
-  const int h = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int dd = blockIdx.y * 32 + lane;
-  const bool has_dim = dd < d;
-  const int lo = static_cast<int>(static_cast<long long>(n_parts) * warp / kCombineWarps);
-  const int hi = static_cast<int>(static_cast<long long>(n_parts) * (warp + 1) / kCombineWarps);
-  const size_t stride = static_cast<size_t>(qh) * d;
-  float M = -INFINITY, L = 0.f, A = 0.f;
-  for (int base = lo; base < hi; base += 32) {
-    const int p = base + lane;
-    float mp = -INFINITY, lp = 0.f;
-    if (p < hi) {
-      const float2 ml =
-          *reinterpret_cast<const float2*>(part_ml + (static_cast<size_t>(p) * qh + h) * 2);
-      mp = ml.x;
-      lp = ml.y;
-    }
-    const float* row = part_acc + (static_cast<size_t>(base) * qh + h) * d + dd;
-    float v[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = (base + j < hi && has_dim) ? row[j * stride] : 0.f;
-    float cm = mp;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
-    const float nm = fmaxf(M, cm);
-    if (nm == -INFINITY) continue;  // only empty parts so far
-    const float keep = exp2f(M - nm);  // 0 while M is -inf
-    const float wp = mp == -INFINITY ? 0.f : exp2f(mp - nm);
-    float ls = wp * lp;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
-    L = fmaf(L, keep, ls);
-    A *= keep;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) A = fmaf(__shfl_sync(0xffffffffu, wp, j), v[j], A);
-    M = nm;
-  }
-  if (lane == 0) {
-    wm[warp] = M;
-    wl[warp] = L;
-  }
-  wacc[warp][lane] = A;
-  __syncthreads();
-  if (warp != 0) return;
-  float mx = -INFINITY;
-#pragma unroll
-  for (int w = 0; w < kCombineWarps; ++w) mx = fmaxf(mx, wm[w]);
-  float ls = 0.f, t = 0.f;
-#pragma unroll
-  for (int w = 0; w < kCombineWarps; ++w) {
-    const float ww = wm[w] == -INFINITY ? 0.f : exp2f(wm[w] - mx);
-    ls = fmaf(ww, wl[w], ls);
-    t = fmaf(ww, wacc[w][lane], t);
-  }
-  const bool empty = (mx == -INFINITY) || !(ls > 0.f);
-  if (has_dim) out[static_cast<size_t>(h) * d + dd] = empty ? 0.f : t / ls;
-  if (blockIdx.y == 0 && lane == 0) lse[h] = empty ? -INFINITY : (mx + log2f(ls)) * kLn2;
+  combine_slice(part_acc, part_ml, n_parts, qh, d, blockIdx.x, blockIdx.y, out, lse);
 }
 
 // grid = (query_heads, ceil(d / blockDim)); outs [n, qh, d], lses [n, qh].

@@ -1,0 +1,86 @@
+// Split-KV combine of one (query head, 32-dim slice): shared by the standalone combine kernel
+// and the tail of the streaming decode kernel. Parts hold (m in log2 units, l, unnormalised
+// acc) per query head; the result is the normalised output and the natural-log LSE that
+// kvssd's backends return (src/kvssd/backends/base.py:76-81, docs/v0.2-design.md:51-62).
+#pragma once
+
+#include <stdint.h>
+
+namespace kvb {
+
+constexpr int kCombineWarps = 16;   // the caller's block is 32 * kCombineWarps threads
+constexpr float kLn2 = 0.693147180559945309f;
+
+// Warp w folds the contiguous part range [w*n/W, (w+1)*n/W) for dims [32*chunk, 32*chunk+32),
+// 32 parts per batch: all of a batch's loads (lane j: part j's m and l; every lane: its dim of
+// the 32 parts' rows) are issued before any of them is used, so a batch costs one round trip
+// to L2. Part weights reach the other lanes by shuffle; the W warp states are merged through
+// shared memory. Every thread of the block must call it (it synchronises the block). Parts are
+// read with L2-coherent loads (ld.global.cg): they may have been written by other CTAs of the
+// same grid.
+__device__ __forceinline__ void combine_slice(const float* __restrict__ part_acc,
+                                              const float* __restrict__ part_ml, int n_parts,
+                                              int qh, int d, int h, int chunk,
+                                              float* __restrict__ out, float* __restrict__ lse) {
+  __shared__ float wm[kCombineWarps], wl[kCombineWarps], wacc[kCombineWarps][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int dd = chunk * 32 + lane;
+  const bool has_dim = dd < d;
+  const int lo = static_cast<int>(static_cast<long long>(n_parts) * warp / kCombineWarps);
+  const int hi = static_cast<int>(static_cast<long long>(n_parts) * (warp + 1) / kCombineWarps);
+  const size_t stride = static_cast<size_t>(qh) * d;
+  float M = -INFINITY, L = 0.f, A = 0.f;
+  for (int base = lo; base < hi; base += 32) {
+    const int p = base + lane;
+    float mp = -INFINITY, lp = 0.f;
+    if (p < hi) {
+      const float2 ml =
+          __ldcg(reinterpret_cast<const float2*>(part_ml + (static_cast<size_t>(p) * qh + h) * 2));
+      mp = ml.x;
+      lp = ml.y;
+    }
+    const float* row = part_acc + (static_cast<size_t>(base) * qh + h) * d + dd;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (base + j < hi && has_dim) ? __ldcg(row + j * stride) : 0.f;
+    float cm = mp;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+    const float nm = fmaxf(M, cm);
+    if (nm == -INFINITY) continue;  // only empty parts so far
+    const float keep = exp2f(M - nm);  // 0 while M is -inf
+    const float wp = mp == -INFINITY ? 0.f : exp2f(mp - nm);
+    float ls = wp * lp;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+    L = fmaf(L, keep, ls);
+    A *= keep;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) A = fmaf(__shfl_sync(0xffffffffu, wp, j), v[j], A);
+    M = nm;
+  }
+  if (lane == 0) {
+    wm[warp] = M;
+    wl[warp] = L;
+  }
+  wacc[warp][lane] = A;
+  __syncthreads();
+  if (warp == 0) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kCombineWarps; ++w) mx = fmaxf(mx, wm[w]);
+    float ls = 0.f, t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCombineWarps; ++w) {
+      const float ww = wm[w] == -INFINITY ? 0.f : exp2f(wm[w] - mx);
+      ls = fmaf(ww, wl[w], ls);
+      t = fmaf(ww, wacc[w][lane], t);
+    }
+    const bool empty = (mx == -INFINITY) || !(ls > 0.f);
+    if (has_dim) out[static_cast<size_t>(h) * d + dd] = empty ? 0.f : t / ls;
+    if (chunk == 0 && lane == 0) lse[h] = empty ? -INFINITY : (mx + log2f(ls)) * kLn2;
+  }
+  __syncthreads();  // the shared arrays may be reused by the caller's next slice
+}
+
+}  // namespace kvb

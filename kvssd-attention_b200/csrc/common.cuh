@@ -29,7 +29,15 @@ enum QueryDtype : int { kQF32 = 0, kQF16 = 1, kQBF16 = 2, kQF64 = 3 };
 enum DeviceStatusBits : unsigned {
   kDevBadBlockIndex = 1u,   // a block-table entry outside [0, n_pool_blocks)
   kDevBadValidCount = 2u,   // a valid_tokens entry outside [0, block_tokens]
+  kDevCombineTimeout = 4u,  // a fused combine gave up waiting for the other CTAs' parts
 };
+
+// GPU-scope acquire load (pairs with __threadfence + atomicAdd on the writer side).
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ float load_query(const void* q, int dtype, long long idx) {
   switch (dtype) {

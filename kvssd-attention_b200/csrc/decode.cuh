@@ -39,6 +39,11 @@ struct DecodeArgs {
   float* part_acc;    // [n_parts, qh, d] unnormalised sum p*v
   float* part_ml;     // [n_parts, qh, 2]  (running max in log2 domain, sum of p)
   unsigned* status;   // device status word (DeviceStatusBits)
+  // Fused combine (streaming kernel): the last CTAs to finish fold all parts into out/lse.
+  int fuse_combine;
+  unsigned* tickets;  // [0] CTAs that wrote their part, [1] combiners done; zero between calls
+  float* out;         // [qh, d] normalised output
+  float* lse;         // [qh] natural-log LSE
 };
 
 // Resolves slot -> (pool block, clamped valid count) with a per-warp register cache of 32

@@ -34,7 +34,9 @@
 //   sm_scale*log2(e)) with a lazily updated running max: the max and the accumulator move only
 //   when a score exceeds the running max by 2^8, detected with one warp vote per tile.
 // The CTA finally merges the wph warps of each head through shared memory and writes one
-// (m, l, acc) part per query head for the combine kernel.
+// (m, l, acc) part per query head; with the fused combine the last CTAs to finish then fold
+// the parts into the output (otherwise the combine kernel does).
+#include "combine.cuh"
 #include "decode_tc.cuh"
 
 namespace kvb {
@@ -115,6 +117,56 @@ struct WarpFeed {
   }
 };
 
+// Bounds of a fused-combine wait: one second of GPU time, and a poll count as a second guard.
+constexpr unsigned long long kCombineWaitNs = 1000000000ull;
+constexpr unsigned kCombineMaxPolls = 1u << 26;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Fused split-KV combine at the end of the decode grid (launched cooperatively, so all CTAs
+// are co-resident). Every CTA publishes its part and signals its arrival with one release
+// add; the n_comb highest-numbered CTAs (one per (query head, 32-dim) slice, or fewer when the
+// grid is smaller) wait until all n_splits parts have arrived and fold one or more slices
+// each. The wait is bounded: on timeout the CTA flags kDevCombineTimeout and carries on. The
+// last combiner to finish resets both counters, so the header is zero again for the next call.
+template <int D>
+__device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a) {
+  __syncthreads();  // every warp's part stores precede the CTA's release below
+  constexpr int kChunks = (D + 31) / 32;
+  const int n_slices = a.qh * kChunks;
+  const int n_comb = min(a.n_splits, n_slices);
+  const int k = static_cast<int>(blockIdx.x) - (a.n_splits - n_comb);
+  if (threadIdx.x == 0) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.tickets) : "memory");
+    if (k >= 0) {
+      const unsigned long long t0 = global_ns();
+      unsigned polls = 0;
+      while (ld_acquire_gpu(a.tickets) < static_cast<unsigned>(a.n_splits)) {
+        if (++polls > kCombineMaxPolls || global_ns() - t0 > kCombineWaitNs) {
+          atomicOr(a.status, kDevCombineTimeout);
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+  }
+  if (k < 0) return;
+  __syncthreads();
+  for (int sl = k; sl < n_slices; sl += n_comb)
+    combine_slice(a.part_acc, a.part_ml, a.n_splits, a.qh, D, sl / kChunks, sl % kChunks, a.out,
+                  a.lse);
+  if (threadIdx.x == 0) {
+    if (atomicAdd(a.tickets + 1, 1u) == static_cast<unsigned>(n_comb) - 1) {
+      atomicExch(a.tickets, 0u);
+      atomicExch(a.tickets + 1, 0u);
+    }
+  }
+}
+
 template <int KVH, int GROUP>
 __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const DecodeArgs a) {
   constexpr int D = 128, BITS = 4, G = D / GROUP, MT = D / 16, DEPTH = kAsyncDepth;
@@ -128,6 +180,10 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
   static_assert(G == 4 || G == 2, "scale rows must be whole 4-byte words");
   static_assert(DEPTH <= 32, "partial-tile flags are one bit per stage");
   extern __shared__ __align__(128) uint8_t smem[];
+  // Launched with programmatic stream serialization: wait for the preceding grid before the
+  // first global access (it may have produced the query or the KV), and let the next decode
+  // launch early so its launch latency overlaps this grid's tail.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, c = lane & 3;
@@ -345,47 +401,49 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
       for (int e = 0; e < 4; ++e) dst[(4 + 4 * k + e) * 32] = acc[k][e];
   }
   __syncthreads();
-  if (sub > 0) return;
-  for (int o = 1; o < WPH; ++o) {
-    const float* src = buf + static_cast<size_t>((o - 1) * KVH + h) * kFields * 32 + lane;
+  if (sub == 0) {
+    for (int o = 1; o < WPH; ++o) {
+      const float* src = buf + static_cast<size_t>((o - 1) * KVH + h) * kFields * 32 + lane;
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const float mo = src[hh * 32], lo = src[(2 + hh) * 32];
-      const float mn = fmaxf(m_run[hh], mo);
-      const float a0 = mn == -INFINITY ? 0.f : fast_exp2(m_run[hh] - mn);
-      const float a1 = mn == -INFINITY ? 0.f : fast_exp2(mo - mn);
-      m_run[hh] = mn;
-      l_run[hh] = l_run[hh] * a0 + lo * a1;
+      for (int hh = 0; hh < 2; ++hh) {
+        const float mo = src[hh * 32], lo = src[(2 + hh) * 32];
+        const float mn = fmaxf(m_run[hh], mo);
+        const float a0 = mn == -INFINITY ? 0.f : fast_exp2(m_run[hh] - mn);
+        const float a1 = mn == -INFINITY ? 0.f : fast_exp2(mo - mn);
+        m_run[hh] = mn;
+        l_run[hh] = l_run[hh] * a0 + lo * a1;
 #pragma unroll
-      for (int k = 0; k < MT; ++k) {
-        acc[k][hh] = acc[k][hh] * a0 + src[(4 + 4 * k + hh) * 32] * a1;
-        acc[k][2 + hh] = acc[k][2 + hh] * a0 + src[(4 + 4 * k + 2 + hh) * 32] * a1;
+        for (int k = 0; k < MT; ++k) {
+          acc[k][hh] = acc[k][hh] * a0 + src[(4 + 4 * k + hh) * 32] * a1;
+          acc[k][2 + hh] = acc[k][2 + hh] * a0 + src[(4 + 4 * k + 2 + hh) * 32] * a1;
+        }
       }
     }
-  }
-  // ---- this CTA's part; O^T row g of M-tile (j, k2) is dim 32j + 4g + 2k2, row g+8 the next
+    // ---- this CTA's part; O^T row g of M-tile (j, k2) is dim 32j + 4g + 2k2, row g+8 the next
 #pragma unroll
-  for (int o = 4; o < 32; o <<= 1) {
-    l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], o);
-    l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], o);
-  }
-#pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    const int n = 2 * c + hh;
-    if (n >= nq) continue;
-    const size_t row = static_cast<size_t>(blockIdx.x) * a.qh + (q0 + n);
-    if (g == 0) {
-      a.part_ml[row * 2 + 0] = m_run[hh];
-      a.part_ml[row * 2 + 1] = l_run[hh];
+    for (int o = 4; o < 32; o <<= 1) {
+      l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], o);
+      l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], o);
     }
-    float* dst = a.part_acc + row * D + 4 * g;
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int hh = 0; hh < 2; ++hh) {
+      const int n = 2 * c + hh;
+      if (n >= nq) continue;
+      const size_t row = static_cast<size_t>(blockIdx.x) * a.qh + (q0 + n);
+      if (g == 0) {
+        a.part_ml[row * 2 + 0] = m_run[hh];
+        a.part_ml[row * 2 + 1] = l_run[hh];
+      }
+      float* dst = a.part_acc + row * D + 4 * g;
 #pragma unroll
-      for (int k2 = 0; k2 < 2; ++k2)
-        *reinterpret_cast<float2*>(dst + 32 * j + 2 * k2) =
-            make_float2(acc[2 * j + k2][hh], acc[2 * j + k2][2 + hh]);
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int k2 = 0; k2 < 2; ++k2)
+          *reinterpret_cast<float2*>(dst + 32 * j + 2 * k2) =
+              make_float2(acc[2 * j + k2][hh], acc[2 * j + k2][2 + hh]);
+    }
   }
+  if (a.fuse_combine) fused_combine_tail<D>(a);
 }
 
 using DecodeKernel = void (*)(const DecodeArgs);

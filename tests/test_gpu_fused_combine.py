@@ -1,0 +1,105 @@
+"""The streaming kernel's fused split-KV combine: equality with the two-launch path, the
+arrival counters returning to zero, and the bounded wait (a planted counter value that can
+never be reached makes the combining CTAs give up after about a second and flag status bit 4;
+nothing faults or hangs)."""
+
+from __future__ import annotations
+
+import math
+import time
+
+import pytest
+import torch
+
+from kvssd_b200 import _native, ops
+from kvssd_b200.workloads import WORKLOADS, make_layer
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+TICKETS = 128  # byte offset of the two arrival counters in the workspace header
+
+
+@pytest.fixture(scope="module")
+def layer():
+    w = WORKLOADS["c1"]
+    cpu = make_layer(w, 0, "cpu")
+    return w, [t.to(DEV) for t in (cpu.query, cpu.packed_k, cpu.packed_v, cpu.scales_k,
+                                   cpu.scales_v, cpu.valid_tokens)]
+
+
+def _workspace(w, tensors) -> torch.Tensor:
+    q, kp = tensors[0], tensors[1]
+    n, bt, kvh, _ = kp.shape
+    import ctypes
+    need = ctypes.c_size_t()
+    _native.check(_native.library().kvssd_b200_decode_workspace_size(
+        n, bt, q.shape[0], kvh, q.shape[1], w.bits, w.group_size, ctypes.byref(need)), "size")
+    return torch.zeros(need.value, dtype=torch.uint8, device=DEV)
+
+
+def _abi_decode(w, tensors, ws):
+    q, kp, vp, ks, vs, valid = tensors
+    n, bt, kvh, _ = kp.shape
+    qh, d = q.shape
+    out = torch.full((qh, d), float("nan"), device=DEV)
+    lse = torch.full((qh,), float("nan"), device=DEV)
+    _native.check(_native.library().kvssd_b200_decode(
+        q.data_ptr(), _native.Q_F16, kp.data_ptr(), vp.data_ptr(), ks.data_ptr(), vs.data_ptr(),
+        valid.data_ptr(), None, n, n, bt, qh, kvh, d, w.bits, w.group_size,
+        1.0 / math.sqrt(d), out.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws.numel(),
+        torch.cuda.current_stream().cuda_stream), "kvssd_b200_decode")
+    return out, lse
+
+
+def _status(ws) -> int:
+    import ctypes
+    st = ctypes.c_uint()
+    _native.library().kvssd_b200_read_status(ws.data_ptr(), 1, ctypes.byref(st),
+                                             torch.cuda.current_stream().cuda_stream)
+    return st.value
+
+
+def test_streaming_plan_fuses_the_combine(layer):
+    w, t = layer
+    plan = ops.decode_plan(t[1].shape[0], w.block_tokens, w.query_heads, w.kv_heads, w.head_dim,
+                           w.bits, w.group_size)
+    assert plan["kernel"] == "tensor_core_stream"
+
+
+def test_fused_combine_equals_two_launch_combine_and_resets_counters(layer):
+    w, t = layer
+    ws = _workspace(w, t)
+    fused = _abi_decode(w, t, ws)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(ws[TICKETS:TICKETS + 8]) == 0
+    assert _status(ws) == 0
+    args = (t[0], *t[1:], w.bits, w.group_size, 1.0 / math.sqrt(w.head_dim))
+    n_parts, wsp = ops.decode_split(*args)
+    two = ops.decode_combine(wsp, n_parts, w.query_heads, w.head_dim)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(fused[0], two[0], atol=1e-6, rtol=1e-6)
+    torch.testing.assert_close(fused[1], two[1], atol=1e-6, rtol=1e-6)
+    again = _abi_decode(w, t, ws)  # the counters were back at zero for the second call
+    torch.cuda.synchronize()
+    assert torch.equal(again[0], fused[0]) and torch.equal(again[1], fused[1])
+
+
+def test_fused_combine_wait_is_bounded_and_flagged(layer):
+    w, t = layer
+    ws = _workspace(w, t)
+    # Planted arrival count 2^32 - 100: after every CTA arrives the counter has wrapped to a
+    # value below the number of CTAs, so the combining CTAs can never see all parts.
+    ws[TICKETS:TICKETS + 4] = torch.tensor([0x9C, 0xFF, 0xFF, 0xFF], dtype=torch.uint8)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    _abi_decode(w, t, ws)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    assert _status(ws) & 4
+    assert elapsed < 30
+    ws.zero_()
+    out, lse = _abi_decode(w, t, ws)
+    ref = ops.decode(*t, w.bits, w.group_size, 1.0 / math.sqrt(w.head_dim))
+    torch.cuda.synchronize()
+    assert _status(ws) == 0
+    torch.testing.assert_close(out, ref[0], atol=1e-6, rtol=1e-6)
