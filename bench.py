@@ -9,9 +9,10 @@ and microseconds per layer-decode, for the 128K-token INT4 GQA configuration: 1 
   python bench.py --impl reference [--steps K] [--warmup W]      # reference CPU decode
 
 N > 1 runs one rank per GPU (launched by torch.distributed.run): the context is N x 131072
-tokens split by token-block ranges, each rank decodes its 1024 blocks and the normalised
-(out, lse) pairs are exchanged with one NCCL all-gather and merged exactly on every rank
-(weak scaling; at N = 8 this is the 1M-token configuration).
+tokens split by token-block ranges; each rank decodes its 1024 blocks, and the same kernel
+pushes its combined (out, lse) slices to every rank over NVLink peer stores and merges all
+ranks' slices exactly, so a step is one kernel per rank (weak scaling; at N = 8 this is the
+1M-token configuration).
 """
 
 from __future__ import annotations
@@ -341,7 +342,13 @@ def run_ours(args) -> None:
                          w.bits, w.group_size, scale)
 
     split_ms = timed(split_only, args.steps, 3, graph=not args.eager)
-    kernel_ms = timed(local_decode, args.steps, 3, graph=not args.eager) if fused else split_ms
+    peer = sharded is not None and sharded._peer is not None
+    if peer:  # the timed step is exactly one kernel per rank: decode + combine + exchange
+        kernel_ms = ms
+    elif fused:
+        kernel_ms = timed(local_decode, args.steps, 3, graph=not args.eager)
+    else:
+        kernel_ms = split_ms
     kernel_name = {"tensor_core_stream": "async_decode_kernel", "tensor_core_regs": "tc_decode_kernel",
                    "generic": "simt_decode_kernel"}[plan["kernel"]]
     peak, peak_kind = peaks()
@@ -379,12 +386,14 @@ def run_ours(args) -> None:
         cpu = cpu_oracle_run(args.cpu_seconds)
     torch.cuda.synchronize(device)
     graphs.clear()  # graphs that hold NCCL calls go before the process group
+    if sharded is not None:
+        sharded.close()  # collective: unmaps the peers' exchange buffers
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
-    launches_per_step = (1 if fused else 2) + (1 if world > 1 else 0)
+    launches_per_step = 1 if fused else 2 + (1 if world > 1 else 0)
     record = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
@@ -393,7 +402,9 @@ def run_ours(args) -> None:
             "workload": (f"{WORKLOAD}: 1 layer x 131072 tokens per GPU, INT4 group 32 FP16 "
                          "scales, 8 KV heads x 128, 32 query heads (GQA 4), block 128, AllBlocks"
                          + (f"; {world} GPUs split one {world * 131072}-token context by "
-                            "token-block ranges, NCCL all-gather + exact merge" if world > 1 else "")),
+                            "token-block ranges; each rank's decode kernel pushes its combined "
+                            "slices to every rank over NVLink peer stores and merges them exactly "
+                            "(one kernel per rank per step)" if world > 1 else "")),
             "us_per_layer_decode": ms * 1e3,
             "packed_kv_bytes_per_gpu": nbytes,
             "hbm_peak_gbs": peak,
@@ -410,14 +421,15 @@ def run_ours(args) -> None:
                      "frac": achieved / peak, "traffic": traffic,
                      "kernel": f"{kernel_name}<{w.kv_heads},{w.group_size}> "
                                f"({plan['n_splits']} CTAs, split-KV stream"
-                               + ("; combine fused in the kernel tail)" if fused else
-                                  "; combine kernel excluded)"),
+                               + ("; combine and NVLink exchange fused in the kernel tail)"
+                                  if peer else "; combine fused in the kernel tail)" if fused
+                                  else "; combine kernel excluded)"),
                      "kernel_us": kernel_ms * 1e3,
                      "split_only_us": split_ms * 1e3,
                      "peak_kind": f"{peak_kind} (burst copy)"},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                "path": ("ShardedDecoder.run (C ABI decode, NCCL all-gather, merge kernel)"
+                "path": ("ShardedDecoder.run (C ABI kvssd_b200_decode_exchange over NVLink)"
                          if world > 1 else "B200AttentionBackend.run (C ABI)")
                         + " from pinned host buffers"},
         "gpu_launches": args.steps * launches_per_step,

@@ -153,10 +153,57 @@ KVSSD_B200_API int kvssd_b200_decode_plan(int n_sel_blocks, int block_tokens, in
  * measurements and tests; AUTO restores the default. No reference counterpart. */
 KVSSD_B200_API int kvssd_b200_set_path_override(int path);
 
+/* Size of a CUDA IPC memory handle (cudaIpcMemHandle_t). */
+#define KVSSD_B200_IPC_HANDLE_BYTES 64
+
+/* Bytes of one rank's exchange buffer for kvssd_b200_decode_exchange with `world` ranks.
+ * No reference counterpart (the reference runs on one device). */
+KVSSD_B200_API int kvssd_b200_exchange_bytes(int world, int query_heads, int head_dim,
+                                             size_t* bytes);
+
+/* Allocates and zeroes an exchange buffer on the current device (cudaMalloc; 256-byte
+ * aligned), re-zeroes it (synchronously, e.g. after an exchange timeout) and frees it. Call
+ * outside any stream capture. */
+KVSSD_B200_API int kvssd_b200_exchange_alloc(size_t bytes, void** buffer);
+KVSSD_B200_API int kvssd_b200_exchange_clear(void* buffer, size_t bytes);
+KVSSD_B200_API int kvssd_b200_exchange_free(void* buffer);
+
+/* CUDA IPC export of an exchange buffer into a KVSSD_B200_IPC_HANDLE_BYTES handle, import of a
+ * peer process's handle (peer access enabled lazily) and release of the import. */
+KVSSD_B200_API int kvssd_b200_ipc_handle(void* buffer, void* handle);
+KVSSD_B200_API int kvssd_b200_ipc_open(const void* handle, void** buffer);
+KVSSD_B200_API int kvssd_b200_ipc_close(void* buffer);
+
+/* Multi-GPU decode of one context split by token-block ranges, one process per GPU: the
+ * decode of this rank's blocks, its split-KV combine and the exact cross-rank merge in ONE
+ * kernel. Each combined (query head, 32-dim) slice is pushed with peer stores over NVLink into
+ * every rank's exchange buffer (`buffers`: `world` device pointers, this rank's own at index
+ * `rank`, peers' from kvssd_b200_ipc_open) and merged from there once all ranks' copies of the
+ * slice have arrived; every rank ends with the same out/lse for the whole context. Replaces the
+ * per-chunk pairwise merges of the reference pipeline (src/kvssd/pipeline.py:147-153,
+ * merge_attention_chunks at src/kvssd/attention.py:91-102) when the chunks live on different
+ * GPUs. Every rank makes the same sequence of calls; the calls are numbered on the device (the
+ * buffer's header), so they may be captured in a CUDA graph. A rank that does not arrive
+ * within about a second makes the others flag status bit 8 (kvssd_b200_read_status) and
+ * return; the ranks' call numbers then differ, and the group re-zeroes its buffers (after a
+ * barrier) before the next call. Requires the streaming kernel's shapes (INT4, head_dim 128,
+ * group 32/64, 16-byte aligned operands) and a cooperative launch; other arguments as
+ * kvssd_b200_decode. No reference counterpart. */
+KVSSD_B200_API int kvssd_b200_decode_exchange(const void* query, int query_dtype,
+                      const uint8_t* packed_k, const uint8_t* packed_v,
+                      const uint16_t* scales_k, const uint16_t* scales_v,
+                      const int32_t* valid_tokens, const int32_t* block_table,
+                      int n_pool_blocks, int n_sel_blocks, int block_tokens, int query_heads,
+                      int kv_heads, int head_dim, int bits, int group_size, float sm_scale,
+                      int rank, int world, void* const* buffers, float* out,
+                      float* lse, void* workspace, size_t workspace_bytes,
+                      kvssd_b200_stream_t stream);
+
 /* Reads (synchronising `stream`) and optionally clears the device status word of a decode
  * workspace; *device_status receives the OR of flagged conditions (1 = block-table entry out
  * of range, 2 = valid_tokens entry out of [0, block_tokens], 4 = a fused combine gave up after
- * waiting about a second for the other CTAs' parts; out/lse of that call are invalid). Returns
+ * waiting about a second for the other CTAs' parts, 8 = a cross-GPU exchange gave up waiting
+ * for another rank; out/lse of a timed-out call are invalid). Returns
  * KVSSD_B200_ERR_DEVICE_STATUS when it is nonzero. No reference counterpart. */
 KVSSD_B200_API int kvssd_b200_read_status(void* workspace, int clear, unsigned* device_status,
                            kvssd_b200_stream_t stream);

@@ -345,6 +345,9 @@ int prepare_decode(const void* query, int query_dtype, const uint8_t* packed_k,
   a.fuse_combine = 0;
   a.out = nullptr;
   a.lse = nullptr;
+  a.xworld = 0;
+  a.xrank = 0;
+  for (int r = 0; r < kMaxExchangeRanks; ++r) a.xpeers[r] = nullptr;
   a.part_ml = reinterpret_cast<float*>(ws + kHeaderBytes);
   a.part_acc = a.part_ml + static_cast<size_t>(p.n_parts) * query_heads * 2;
   return KVSSD_B200_OK;
@@ -523,6 +526,104 @@ int kvssd_b200_decode_combine(const void* workspace, int n_parts, int query_head
   cudaError_t e = launch_combine(acc, ml, n_parts, query_heads, head_dim, out, lse,
                                  reinterpret_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "combine launch");
+}
+
+int kvssd_b200_exchange_bytes(int world, int query_heads, int head_dim, size_t* bytes) {
+  if (!bytes) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "bytes must not be NULL");
+  if (world < 1 || world > kMaxExchangeRanks)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "exchange supports 1 to 8 ranks");
+  if (query_heads < 1 || head_dim < 1 || head_dim > 256)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "bad exchange geometry");
+  *bytes = exchange_bytes(world, query_heads * ((head_dim + 31) / 32));
+  return KVSSD_B200_OK;
+}
+
+int kvssd_b200_exchange_alloc(size_t bytes, void** buffer) {
+  if (!buffer || bytes == 0) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "bad exchange buffer request");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "exchange buffer allocation");
+  e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "exchange buffer clear");
+  }
+  *buffer = p;
+  return KVSSD_B200_OK;
+}
+
+int kvssd_b200_exchange_clear(void* buffer, size_t bytes) {
+  if (!buffer) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "NULL pointer");
+  cudaError_t e = cudaMemset(buffer, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "exchange buffer clear");
+}
+
+int kvssd_b200_exchange_free(void* buffer) {
+  cudaError_t e = cudaFree(buffer);
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "exchange buffer free");
+}
+
+int kvssd_b200_ipc_handle(void* buffer, void* handle) {
+  if (!buffer || !handle) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "NULL pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, buffer);
+  if (e != cudaSuccess) return cuda_fail(e, "IPC handle");
+  static_assert(sizeof(h) == KVSSD_B200_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  return KVSSD_B200_OK;
+}
+
+int kvssd_b200_ipc_open(const void* handle, void** buffer) {
+  if (!buffer || !handle) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "NULL pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(buffer, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "IPC open");
+}
+
+int kvssd_b200_ipc_close(void* buffer) {
+  cudaError_t e = cudaIpcCloseMemHandle(buffer);
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "IPC close");
+}
+
+int kvssd_b200_decode_exchange(const void* query, int query_dtype, const uint8_t* packed_k,
+                               const uint8_t* packed_v, const uint16_t* scales_k,
+                               const uint16_t* scales_v, const int32_t* valid_tokens,
+                               const int32_t* block_table, int n_pool_blocks, int n_sel_blocks,
+                               int block_tokens, int query_heads, int kv_heads, int head_dim,
+                               int bits, int group_size, float sm_scale, int rank, int world,
+                               void* const* buffers, float* out, float* lse,
+                               void* workspace, size_t workspace_bytes,
+                               kvssd_b200_stream_t stream) {
+  if (!out || !lse || !buffers)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "pointers must not be NULL");
+  if (world < 1 || world > kMaxExchangeRanks || rank < 0 || rank >= world)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "rank/world outside 1 to 8 ranks");
+  for (int r = 0; r < world; ++r)
+    if (!buffers[r] || (reinterpret_cast<uintptr_t>(buffers[r]) & 15u))
+      return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "exchange buffers must be 16-byte aligned");
+  DecodeArgs a;
+  Plan p;
+  int st = prepare_decode(query, query_dtype, packed_k, packed_v, scales_k, scales_v, valid_tokens,
+                          block_table, n_pool_blocks, n_sel_blocks, block_tokens, query_heads,
+                          kv_heads, head_dim, bits, group_size, sm_scale, workspace,
+                          workspace_bytes, a, p);
+  if (st) return st;
+  if (!p.streaming)
+    return fail(KVSSD_B200_ERR_UNSUPPORTED,
+                "the fused exchange needs the streaming kernel (INT4, head_dim 128, group 32/64, "
+                "16-byte aligned operands)");
+  a.xworld = world;
+  a.xrank = rank;
+  for (int r = 0; r < world; ++r) a.xpeers[r] = static_cast<uint8_t*>(buffers[r]);
+  a.fuse_combine = 1;
+  a.out = out;
+  a.lse = lse;
+  st = launch_split(a, p, reinterpret_cast<cudaStream_t>(stream));
+  if (st == KVSSD_B200_ERR_UNSUPPORTED)
+    return fail(st, "the fused exchange needs a cooperative launch of the whole grid");
+  return st;
 }
 
 int kvssd_b200_read_status(void* workspace, int clear, unsigned* device_status,

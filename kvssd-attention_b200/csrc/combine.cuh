@@ -18,10 +18,12 @@ constexpr float kLn2 = 0.693147180559945309f;
 // shared memory. Every thread of the block must call it (it synchronises the block). Parts are
 // read with L2-coherent loads (ld.global.cg): they may have been written by other CTAs of the
 // same grid.
-__device__ __forceinline__ void combine_slice(const float* __restrict__ part_acc,
-                                              const float* __restrict__ part_ml, int n_parts,
-                                              int qh, int d, int h, int chunk,
-                                              float* __restrict__ out, float* __restrict__ lse) {
+// Result in warp 0: *o = the normalised output of dim 32 * chunk + lane (0 when the head saw
+// no token), *l2 = the slice's LSE in log2 units (-inf when empty). Other warps get nothing.
+__device__ __forceinline__ void combine_slice_result(const float* __restrict__ part_acc,
+                                                     const float* __restrict__ part_ml,
+                                                     int n_parts, int qh, int d, int h,
+                                                     int chunk, float* o, float* l2) {
   __shared__ float wm[kCombineWarps], wl[kCombineWarps], wacc[kCombineWarps][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int dd = chunk * 32 + lane;
@@ -77,10 +79,24 @@ __device__ __forceinline__ void combine_slice(const float* __restrict__ part_acc
       t = fmaf(ww, wacc[w][lane], t);
     }
     const bool empty = (mx == -INFINITY) || !(ls > 0.f);
-    if (has_dim) out[static_cast<size_t>(h) * d + dd] = empty ? 0.f : t / ls;
-    if (chunk == 0 && lane == 0) lse[h] = empty ? -INFINITY : (mx + log2f(ls)) * kLn2;
+    *o = empty ? 0.f : t / ls;
+    *l2 = empty ? -INFINITY : mx + log2f(ls);
   }
   __syncthreads();  // the shared arrays may be reused by the caller's next slice
+}
+
+// The slice's normalised output and natural-log LSE written to out [qh, d] / lse [qh].
+__device__ __forceinline__ void combine_slice(const float* __restrict__ part_acc,
+                                              const float* __restrict__ part_ml, int n_parts,
+                                              int qh, int d, int h, int chunk,
+                                              float* __restrict__ out, float* __restrict__ lse) {
+  float o = 0.f, l2 = -INFINITY;
+  combine_slice_result(part_acc, part_ml, n_parts, qh, d, h, chunk, &o, &l2);
+  const int lane = threadIdx.x & 31, dd = chunk * 32 + lane;
+  if (threadIdx.x < 32) {
+    if (dd < d) out[static_cast<size_t>(h) * d + dd] = o;
+    if (chunk == 0 && lane == 0) lse[h] = l2 * kLn2;
+  }
 }
 
 }  // namespace kvb

@@ -30,7 +30,19 @@ enum DeviceStatusBits : unsigned {
   kDevBadBlockIndex = 1u,   // a block-table entry outside [0, n_pool_blocks)
   kDevBadValidCount = 2u,   // a valid_tokens entry outside [0, block_tokens]
   kDevCombineTimeout = 4u,  // a fused combine gave up waiting for the other CTAs' parts
+  kDevExchangeTimeout = 8u,  // a cross-GPU exchange gave up waiting for another rank's slice
 };
+
+// System-scope relaxed 64-bit load / store (words written across GPUs over NVLink; an
+// aligned 64-bit access is single-copy atomic, so a {value, tag} word arrives whole).
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
 // GPU-scope acquire load (pairs with __threadfence + atomicAdd on the writer side).
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {

@@ -17,6 +17,8 @@
 
 namespace kvb {
 
+constexpr int kMaxExchangeRanks = 8;
+
 struct DecodeArgs {
   const void* q;
   int q_dtype;
@@ -44,7 +46,22 @@ struct DecodeArgs {
   unsigned* tickets;  // [0] CTAs that wrote their part, [1] combiners done; zero between calls
   float* out;         // [qh, d] normalised output
   float* lse;         // [qh] natural-log LSE
+  // Cross-GPU exchange (token-range shards, fused combine only): every combiner pushes its
+  // slice to all ranks' exchange buffers and merges all ranks' slices (0 ranks: no exchange).
+  int xworld;
+  int xrank;
+  uint8_t* xpeers[kMaxExchangeRanks];  // every rank's exchange buffer ([xrank] is local)
 };
+
+// Exchange buffer layout for `world` ranks and n_slices = qh * ceil(d / 32) slices:
+//   header (256 bytes): u32 epoch = number of completed exchange calls on this rank;
+//   then words u64 [2][world][n_slices][33]: {f32 value (low half), u32 epoch (high half)} for
+//   32 normalised dims and the slice's LSE in log2 units. A call's epoch is the header value
+//   + 1; its parity selects the buffer half.
+constexpr size_t kExchangeHeader = 256;
+__host__ __device__ inline size_t exchange_bytes(int world, int n_slices) {
+  return kExchangeHeader + static_cast<size_t>(2) * world * n_slices * 33 * 8;
+}
 
 // Resolves slot -> (pool block, clamped valid count) with a per-warp register cache of 32
 // consecutive slots, so the dependent block-table/valid loads are paid once per 32 blocks.

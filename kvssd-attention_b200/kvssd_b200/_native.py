@@ -20,6 +20,8 @@ ERR_CUDA = 4
 ERR_DEVICE_STATUS = 5
 
 Q_F32, Q_F16, Q_BF16, Q_F64 = 0, 1, 2, 3
+IPC_HANDLE_BYTES = 64
+DEV_BAD_BLOCK, DEV_BAD_VALID, DEV_COMBINE_TIMEOUT, DEV_EXCHANGE_TIMEOUT = 1, 2, 4, 8
 PATH_AUTO, PATH_TENSOR_CORE, PATH_GENERIC, PATH_TENSOR_CORE_REGS = 0, 1, 2, 3
 
 _c_int = ctypes.c_int
@@ -73,6 +75,22 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "kvssd_b200_set_path_override": (_c_int, [_c_int]),
     "kvssd_b200_read_status": (_c_int, [_c_void, _c_int, _c_uint_p, _c_void]),
+    "kvssd_b200_exchange_bytes": (_c_int, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_size)]),
+    "kvssd_b200_exchange_alloc": (_c_int, [_c_size, ctypes.POINTER(_c_void)]),
+    "kvssd_b200_exchange_clear": (_c_int, [_c_void, _c_size]),
+    "kvssd_b200_exchange_free": (_c_int, [_c_void]),
+    "kvssd_b200_ipc_handle": (_c_int, [_c_void, _c_void]),
+    "kvssd_b200_ipc_open": (_c_int, [_c_void, ctypes.POINTER(_c_void)]),
+    "kvssd_b200_ipc_close": (_c_int, [_c_void]),
+    "kvssd_b200_decode_exchange": (
+        _c_int,
+        [
+            _c_void, _c_int, _c_void, _c_void, _c_void, _c_void, _c_void, _c_void,
+            _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+            _c_float, _c_int, _c_int, ctypes.POINTER(_c_void),
+            _c_void, _c_void, _c_void, _c_size, _c_void,
+        ],
+    ),
     "kvssd_b200_merge_chunks": (
         _c_int, [_c_void, _c_void, _c_int, _c_int, _c_int, _c_void, _c_void, _c_void]
     ),

@@ -162,6 +162,42 @@ def decode(
     return out, lse
 
 
+def decode_exchange(query, packed_k, packed_v, scales_k, scales_v, valid_tokens, bits: int,
+                    group_size: int, sm_scale: float, rank: int, world: int,
+                    buffers: list[int], block_table=None, out=None, lse=None,
+                    workspace: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """This rank's share of a multi-GPU decode (token-block-range shards) with the cross-rank
+    merge fused into the kernel (kvssd_b200_decode_exchange); returns the whole context's
+    (out, lse), identical on every rank. ``buffers`` are the ranks' exchange buffers as device
+    addresses valid in this process (see sharding.PeerExchange)."""
+    query, geom = _decode_args(query, packed_k, packed_v, scales_k, scales_v, valid_tokens, bits,
+                               group_size, block_table)
+    device = query.device
+    n_pool, n_sel, bt, qh, kvh, d, _, _ = geom
+    with torch.cuda.device(device):
+        if workspace is None:
+            workspace, stream = _workspace_for(device, geom)
+        else:
+            stream = torch.cuda.current_stream(device)
+        if out is None:
+            out = torch.empty((qh, d), dtype=torch.float32, device=device)
+        if lse is None:
+            lse = torch.empty((qh,), dtype=torch.float32, device=device)
+        _require_cuda("out", out, device, torch.float32)
+        _require_cuda("lse", lse, device, torch.float32)
+        ptrs = (ctypes.c_void_p * len(buffers))(*buffers)
+        status = _native.library().kvssd_b200_decode_exchange(
+            _ptr(query), _QUERY_DTYPES[query.dtype],
+            _ptr(packed_k), _ptr(packed_v), _ptr(scales_k), _ptr(scales_v),
+            _ptr(valid_tokens), _ptr(block_table),
+            n_pool, n_sel, bt, qh, kvh, d, bits, group_size, float(sm_scale),
+            rank, world, ptrs, _ptr(out), _ptr(lse),
+            _ptr(workspace), workspace.numel(), stream.cuda_stream,
+        )
+        _native.check(status, "kvssd_b200_decode_exchange")
+    return out, lse
+
+
 def decode_split(query, packed_k, packed_v, scales_k, scales_v, valid_tokens, bits: int,
                  group_size: int, sm_scale: float, block_table=None) -> tuple[int, torch.Tensor]:
     """Runs only the streaming split-KV kernel; returns (n_parts, workspace).
@@ -208,7 +244,9 @@ def read_device_status(device: torch.device | str | None = None, clear: bool = T
     """Synchronously reads the sticky device status word of the current stream's workspace.
 
     Bit 1: a block-table entry was outside the pool; bit 2: a valid_tokens entry was outside
-    [0, block_tokens]. Such entries are skipped/clamped by the kernels, never dereferenced.
+    [0, block_tokens] (such entries are skipped/clamped by the kernels, never dereferenced);
+    bit 4: a fused combine, bit 8: a cross-GPU exchange gave up waiting (about a second) --
+    the out/lse of that call are invalid.
     """
     device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     stream = torch.cuda.current_stream(device)

@@ -12,9 +12,13 @@
   rank order. kvssd records interleave heads per token (src/kvssd/format.py:165), so a
   head shard is re-laid head-contiguous (``shard_batch_by_heads``) when it is staged.
 
-The exchange is a collective of the caller's process group (NCCL over NVLink for CUDA
-tensors). By default the local decode is libkvssd_b200's kernel writing straight into the
-send buffer and the merge is its N-way merge kernel; a ``decode_fn`` / ``merge_fn`` with the
+Transports. For token shards on CUDA with the streaming kernel's shapes, ``transport="auto"``
+(or ``"peer"``) runs the whole step as ONE kernel per rank (kvssd_b200_decode_exchange): each
+rank's combined slices are pushed with peer stores over NVLink into every rank's exchange
+buffer (mapped through CUDA IPC, see PeerExchange) and merged there, so no collective library
+call and no extra kernel is on the path. Otherwise (``"nccl"``, head shards, other shapes) the
+exchange is an all-gather of the caller's process group (NCCL over NVLink for CUDA tensors)
+and the merge libkvssd_b200's N-way merge kernel; a ``decode_fn`` / ``merge_fn`` with the
 backend ``run`` / merge signatures can be injected instead (the host logic is the same).
 """
 
@@ -32,6 +36,7 @@ DecodeFn = Callable[[torch.Tensor, PackedBatch, float], tuple[torch.Tensor, torc
 MergeFn = Callable[[torch.Tensor, torch.Tensor], tuple[torch.Tensor, torch.Tensor]]
 
 MODES = ("tokens", "heads")
+TRANSPORTS = ("auto", "nccl", "peer")
 
 
 def block_range(n_blocks: int, rank: int, world: int) -> tuple[int, int]:
@@ -81,6 +86,82 @@ def _default_merge() -> MergeFn:
     return ops.merge_chunks
 
 
+class PeerExchange:
+    """Exchange buffers of a process group, mapped into every rank over CUDA IPC.
+
+    Each rank allocates one buffer (kvssd_b200_exchange_bytes for the group size and query
+    geometry) on its GPU, exports an IPC handle, and opens every peer's handle; ``buffers``
+    lists all ranks' buffers as device addresses valid in this process, in rank order.
+    Collective: every rank of ``group`` constructs it (and closes it) at the same point.
+    """
+
+    def __init__(self, group: dist.ProcessGroup | None, device: torch.device, query_heads: int,
+                 head_dim: int):
+        import ctypes
+
+        from . import _native
+
+        lib = _native.library()
+        self.group = group
+        self.device = device
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.query_heads, self.head_dim = query_heads, head_dim
+        nbytes = ctypes.c_size_t()
+        _native.check(lib.kvssd_b200_exchange_bytes(self.world, query_heads, head_dim,
+                                                    ctypes.byref(nbytes)), "exchange_bytes")
+        self.nbytes = nbytes.value
+        local = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(_native.IPC_HANDLE_BYTES)
+        with torch.cuda.device(device):
+            _native.check(lib.kvssd_b200_exchange_alloc(self.nbytes, ctypes.byref(local)),
+                          "exchange_alloc")
+            _native.check(lib.kvssd_b200_ipc_handle(local, handle), "ipc_handle")
+        self._local = local.value
+        handles: list[bytes | None] = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.buffers: list[int] = []
+        self._opened: list[int] = []
+        with torch.cuda.device(device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    self.buffers.append(self._local)
+                    continue
+                peer = ctypes.c_void_p()
+                _native.check(lib.kvssd_b200_ipc_open(h, ctypes.byref(peer)), "ipc_open")
+                self.buffers.append(peer.value)
+                self._opened.append(peer.value)
+
+    def reset(self) -> None:
+        """Re-zeroes every rank's buffer (call numbers and flags) after an exchange timeout
+        left the ranks' call numbers apart. Collective; no exchange may be in flight."""
+        from . import _native
+
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            _native.check(_native.library().kvssd_b200_exchange_clear(self._local, self.nbytes),
+                          "exchange_clear")
+        dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's (collective, after all use)."""
+        from . import _native
+
+        if self._local is None:
+            return
+        lib = _native.library()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                _native.check(lib.kvssd_b200_ipc_close(p), "ipc_close")
+            self._opened.clear()
+            dist.barrier(group=self.group)
+            _native.check(lib.kvssd_b200_exchange_free(self._local), "exchange_free")
+        self._local = None
+
+
 class ShardedDecoder:
     """Decodes this rank's shard and returns the full (out fp32 [QH, D], lse fp32 [QH]) on
     every rank of ``group``.
@@ -92,15 +173,48 @@ class ShardedDecoder:
     """
 
     def __init__(self, mode: str = "tokens", group: dist.ProcessGroup | None = None,
-                 decode_fn: DecodeFn | None = None, merge_fn: MergeFn | None = None):
+                 decode_fn: DecodeFn | None = None, merge_fn: MergeFn | None = None,
+                 transport: str = "auto"):
         if mode not in MODES:
             raise ValueError(f"mode must be one of {MODES}")
+        if transport not in TRANSPORTS:
+            raise ValueError(f"transport must be one of {TRANSPORTS}")
+        if transport == "peer" and (mode != "tokens" or decode_fn is not None):
+            raise ValueError("the peer transport serves token shards with the native decode")
         self.mode = mode
         self.group = group
         self.decode_fn = decode_fn
         self.merge_fn = merge_fn
+        self.transport = transport
         self._send: torch.Tensor | None = None
         self._recv: torch.Tensor | None = None
+        self._peer: PeerExchange | None = None
+        self._peer_out: tuple[torch.Tensor, torch.Tensor] | None = None
+
+    def _use_peer(self, query: torch.Tensor, local: PackedBatch) -> bool:
+        """Token shards on CUDA with the native streaming kernel (INT4, head_dim 128, group
+        32/64, 16-byte aligned operands) and more than one rank: one fused kernel per rank."""
+        if self.transport == "nccl" or self.mode != "tokens" or self.decode_fn is not None:
+            return False
+        if self.world == 1 or query.device.type != "cuda" or local.packed_k.shape[0] == 0:
+            return False
+        from . import ops
+
+        plan = ops.decode_plan(local.packed_k.shape[0], local.packed_k.shape[1], query.shape[0],
+                               local.packed_k.shape[2], query.shape[1], local.bits,
+                               local.group_size)
+        aligned = all(t.data_ptr() % 16 == 0 for t in (local.packed_k, local.packed_v,
+                                                        local.scales_k, local.scales_v))
+        ok = plan["kernel"] == "tensor_core_stream" and aligned
+        if self.transport == "peer" and not ok:
+            raise RuntimeError("peer transport needs the streaming kernel's shapes and alignment")
+        return ok
+
+    def close(self) -> None:
+        """Releases the peer-exchange buffers (collective when the peer transport was used)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     @property
     def world(self) -> int:
@@ -164,8 +278,29 @@ class ShardedDecoder:
             lse_all = recv[:, rows * d :].reshape(world * rows)
             return out_all.clone(), lse_all.clone()
 
+        if self._use_peer(query, local):
+            return self._run_peer(query, local, sm_scale)
         recv = self._gather(self._local(query, local, sm_scale))
         outs = recv[:, : qh * d].reshape(-1, qh, d).contiguous()
         lses = recv[:, qh * d :].contiguous()
         merge = self.merge_fn or _default_merge()
         return merge(outs, lses)
+
+    def _run_peer(self, query: torch.Tensor, local: PackedBatch,
+                  sm_scale: float) -> tuple[torch.Tensor, torch.Tensor]:
+        from . import ops
+
+        qh, d = query.shape
+        if self._peer is None or (self._peer.query_heads, self._peer.head_dim) != (qh, d):
+            if self._peer is not None:
+                self._peer.close()
+            self._peer = PeerExchange(self.group, query.device, qh, d)
+        if self._peer_out is None or self._peer_out[0].shape != (qh, d):
+            self._peer_out = (torch.empty((qh, d), dtype=torch.float32, device=query.device),
+                              torch.empty((qh,), dtype=torch.float32, device=query.device))
+        PackedBatch.validate(local, query)
+        out, lse = self._peer_out
+        return ops.decode_exchange(
+            query, local.packed_k, local.packed_v, local.scales_k, local.scales_v,
+            local.valid_tokens.to(torch.int32).contiguous(), local.bits, local.group_size,
+            sm_scale, self._peer.rank, self._peer.world, self._peer.buffers, out=out, lse=lse)
