@@ -270,8 +270,8 @@ int kvssd_b200_decode_plan(int n_sel_blocks, int block_tokens, int query_heads, 
   const int st = make_plan(g, true, true, p);
   if (st) return st;
   *kernel = p.path == KVSSD_B200_PATH_GENERIC ? KVSSD_B200_PATH_GENERIC
-                                              : (p.streaming ? KVSSD_B200_PATH_TENSOR_CORE
-                                                       : KVSSD_B200_PATH_TENSOR_CORE_REGS);
+            : p.streaming                        ? KVSSD_B200_PATH_TENSOR_CORE
+                                                 : KVSSD_B200_PATH_TENSOR_CORE_REGS;
   *n_splits = p.n_splits;
   *n_parts = p.n_parts;
   return KVSSD_B200_OK;
@@ -373,10 +373,28 @@ int launch_decode(DecodeArgs& a, const Plan& p, float* out, float* lse, cudaStre
   return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "combine launch");
 }
 
+// Raises a kernel's dynamic shared-memory limit (static + dynamic above the 48 KB default
+// needs the opt-in) once per (device, kernel, size), not on every launch.
+cudaError_t ensure_dynamic_smem(DecodeKernel kernel, size_t bytes) {
+  if (bytes <= 16 * 1024) return cudaSuccess;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<int, const void*>, size_t>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  const void* key = reinterpret_cast<const void*>(kernel);
+  for (const auto& d : done)
+    if (d.first.first == dev && d.first.second == key && d.second >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(bytes));
+  if (e == cudaSuccess) done.push_back({{dev, key}, bytes});
+  return e;
+}
+
 int launch_split(DecodeArgs& a, const Plan& p, cudaStream_t s) {
-  if (p.smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(p.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(p.smem));
+  {
+    cudaError_t e = ensure_dynamic_smem(p.kernel, p.smem);
     if (e != cudaSuccess) return cuda_fail(e, "shared-memory attribute");
   }
   if (!p.streaming) {

@@ -15,7 +15,8 @@ constexpr float kLn2 = 0.693147180559945309f;
 // 32 parts per batch: all of a batch's loads (lane j: part j's m and l; every lane: its dim of
 // the 32 parts' rows) are issued before any of them is used, so a batch costs one round trip
 // to L2. Part weights reach the other lanes by shuffle; the W warp states are merged through
-// shared memory. Every thread of the block must call it (it synchronises the block). Parts are
+// shared memory. Every thread of the block must call it (it synchronises the block; warps past
+// the first kCombineWarps only take part in the synchronisation). Parts are
 // read with L2-coherent loads (ld.global.cg): they may have been written by other CTAs of the
 // same grid.
 // Result in warp 0: *o = the normalised output of dim 32 * chunk + lane (0 when the head saw
@@ -28,8 +29,9 @@ __device__ __forceinline__ void combine_slice_result(const float* __restrict__ p
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int dd = chunk * 32 + lane;
   const bool has_dim = dd < d;
-  const int lo = static_cast<int>(static_cast<long long>(n_parts) * warp / kCombineWarps);
-  const int hi = static_cast<int>(static_cast<long long>(n_parts) * (warp + 1) / kCombineWarps);
+  const bool active = warp < kCombineWarps;  // larger blocks: the extra warps only synchronise
+  const int lo = active ? static_cast<int>(static_cast<long long>(n_parts) * warp / kCombineWarps) : 0;
+  const int hi = active ? static_cast<int>(static_cast<long long>(n_parts) * (warp + 1) / kCombineWarps) : 0;
   const size_t stride = static_cast<size_t>(qh) * d;
   float M = -INFINITY, L = 0.f, A = 0.f;
   for (int base = lo; base < hi; base += 32) {
@@ -61,11 +63,13 @@ __device__ __forceinline__ void combine_slice_result(const float* __restrict__ p
     for (int j = 0; j < 32; ++j) A = fmaf(__shfl_sync(0xffffffffu, wp, j), v[j], A);
     M = nm;
   }
-  if (lane == 0) {
-    wm[warp] = M;
-    wl[warp] = L;
+  if (active) {
+    if (lane == 0) {
+      wm[warp] = M;
+      wl[warp] = L;
+    }
+    wacc[warp][lane] = A;
   }
-  wacc[warp][lane] = A;
   __syncthreads();
   if (warp == 0) {
     float mx = -INFINITY;

@@ -33,6 +33,21 @@ enum DeviceStatusBits : unsigned {
   kDevExchangeTimeout = 8u,  // a cross-GPU exchange gave up waiting for another rank's slice
 };
 
+// The G FP16 scales of one (token, KV head) row, loaded as one 8- or 4-byte word.
+template <int G>
+struct ScaleRow {
+  __half s[G];
+  __device__ __forceinline__ void load(const uint8_t* p) {
+    if constexpr (G == 4) {
+      const uint2 w = *reinterpret_cast<const uint2*>(p);
+      memcpy(s, &w, 8);
+    } else {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
+      memcpy(s, &w, 4);
+    }
+  }
+};
+
 // System-scope relaxed 64-bit load / store (words written across GPUs over NVLink; an
 // aligned 64-bit access is single-copy atomic, so a {value, tag} word arrives whole).
 __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {

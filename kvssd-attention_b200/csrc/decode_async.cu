@@ -36,8 +36,8 @@
 // The CTA finally merges the wph warps of each head through shared memory and writes one
 // (m, l, acc) part per query head; with the fused combine the last CTAs to finish then fold
 // the parts into the output (otherwise the combine kernel does).
-#include "combine.cuh"
 #include "decode_tc.cuh"
+#include "fused_tail.cuh"
 
 namespace kvb {
 
@@ -45,19 +45,6 @@ constexpr int kAsyncWarps = 16;
 constexpr int kAsyncThreads = 32 * kAsyncWarps;
 constexpr int kAsyncDepth = 2;  // ring stages per warp (compile-time: cp.async.wait_group N)
 
-template <int G>
-struct ScaleRow {  // the G FP16 scales of one (token, KV head)
-  __half s[G];
-  __device__ __forceinline__ void load(const uint8_t* p) {
-    if constexpr (G == 4) {
-      const uint2 w = *reinterpret_cast<const uint2*>(p);
-      memcpy(s, &w, 8);
-    } else {
-      const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
-      memcpy(s, &w, 4);
-    }
-  }
-};
 
 // D = A * B (zero accumulator start).
 __device__ __forceinline__ void mma_16816_zero(float (&d)[4], uint32_t a0, uint32_t a1,
@@ -116,138 +103,6 @@ struct WarpFeed {
     off += STEP;
   }
 };
-
-// Bounds of a fused-combine wait: one second of GPU time, and a poll count as a second guard.
-constexpr unsigned long long kCombineWaitNs = 1000000000ull;
-constexpr unsigned kCombineMaxPolls = 1u << 26;
-
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Cross-GPU exchange of one combined slice, run by warp 0 of the CTA that combined it (token-
-// range shards of one context, one rank per GPU). Every value travels as one 64-bit word
-// {value, epoch} written with a single store into buffer half (epoch & 1) of every rank's
-// exchange buffer (plain peer stores over NVLink; no fence, since an aligned 64-bit store
-// arrives whole). Each lane then polls the words of its dim from all ranks in its own buffer
-// until their epochs match (bounded: on timeout it flags kDevExchangeTimeout), so a value and
-// its readiness arrive together. The ranks' slices are folded in rank order with the exact
-// merge O = sum_r 2^(L_r - M) O_r / sum_r 2^(L_r - M): every rank computes the same result.
-// Two buffer halves suffice, since a rank can only be one epoch ahead of the slowest reader.
-// The epoch is kept on the device (the buffer's header), so a call captured in a CUDA graph
-// gets a fresh epoch on every replay.
-template <int D>
-__device__ __forceinline__ void exchange_slice(const DecodeArgs& a, unsigned epoch, int slice,
-                                               int n_slices, float o, float l2) {
-  const int lane = threadIdx.x & 31;
-  const int world = a.xworld, par = static_cast<int>(epoch & 1u);
-  const unsigned long long tag = static_cast<unsigned long long>(epoch) << 32;
-  const size_t mine = ((static_cast<size_t>(par) * world + a.xrank) * n_slices + slice) * 33;
-  for (int r = 0; r < world; ++r) {
-    unsigned long long* row =
-        reinterpret_cast<unsigned long long*>(a.xpeers[r] + kExchangeHeader) + mine;
-    st_relaxed_sys_u64(row + lane, tag | __float_as_uint(o));
-    if (lane == 0) st_relaxed_sys_u64(row + 32, tag | __float_as_uint(l2));
-  }
-  const unsigned long long* rows =
-      reinterpret_cast<const unsigned long long*>(a.xpeers[a.xrank] + kExchangeHeader);
-  float vo[kMaxExchangeRanks], vl[kMaxExchangeRanks];
-  const unsigned long long t0 = global_ns();
-  bool timed_out = false;
-#pragma unroll
-  for (int r = 0; r < kMaxExchangeRanks; ++r) {
-    vo[r] = 0.f;
-    vl[r] = -INFINITY;
-    if (r >= world) continue;
-    const unsigned long long* row = rows + ((static_cast<size_t>(par) * world + r) * n_slices + slice) * 33;
-    unsigned long long wo = ld_relaxed_sys_u64(row + lane);
-    unsigned long long wl = lane == 0 ? ld_relaxed_sys_u64(row + 32) : tag;
-    unsigned polls = 0;
-    while (!timed_out && ((wo >> 32) != epoch || (wl >> 32) != epoch)) {
-      if (++polls > kCombineMaxPolls || global_ns() - t0 > kCombineWaitNs) {
-        atomicOr(a.status, kDevExchangeTimeout);
-        timed_out = true;
-        break;
-      }
-      __nanosleep(32);
-      wo = ld_relaxed_sys_u64(row + lane);
-      if (lane == 0) wl = ld_relaxed_sys_u64(row + 32);
-    }
-    vo[r] = __uint_as_float(static_cast<unsigned>(wo));
-    if (lane == 0) vl[r] = __uint_as_float(static_cast<unsigned>(wl));
-  }
-  __syncwarp();
-  float M = -INFINITY;
-#pragma unroll
-  for (int r = 0; r < kMaxExchangeRanks; ++r) {
-    vl[r] = __shfl_sync(0xffffffffu, vl[r], 0);
-    M = fmaxf(M, vl[r]);
-  }
-  float num = 0.f, den = 0.f;
-#pragma unroll
-  for (int r = 0; r < kMaxExchangeRanks; ++r) {
-    const float w = vl[r] == -INFINITY ? 0.f : exp2f(vl[r] - M);
-    num = fmaf(w, vo[r], num);
-    den += w;
-  }
-  constexpr int kChunks = (D + 31) / 32;
-  const int h = slice / kChunks, chunk = slice % kChunks, dd = chunk * 32 + lane;
-  const bool empty = M == -INFINITY || !(den > 0.f);
-  if (dd < D) a.out[static_cast<size_t>(h) * D + dd] = empty ? 0.f : num / den;
-  if (chunk == 0 && lane == 0) a.lse[h] = empty ? -INFINITY : (M + log2f(den)) * kLn2;
-}
-
-// Fused split-KV combine at the end of the decode grid (launched cooperatively, so all CTAs
-// are co-resident). Every CTA publishes its part and signals its arrival with one release
-// add; the n_comb highest-numbered CTAs (one per (query head, 32-dim) slice, or fewer when the
-// grid is smaller) wait until all n_splits parts have arrived and fold one or more slices
-// each. The wait is bounded: on timeout the CTA flags kDevCombineTimeout and carries on. The
-// last combiner to finish resets both counters, so the header is zero again for the next call.
-template <int D>
-__device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned epoch) {
-  __syncthreads();  // every warp's part stores precede the CTA's release below
-  constexpr int kChunks = (D + 31) / 32;
-  const int n_slices = a.qh * kChunks;
-  const int n_comb = min(a.n_splits, n_slices);
-  const int k = static_cast<int>(blockIdx.x) - (a.n_splits - n_comb);
-  if (threadIdx.x == 0) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.tickets) : "memory");
-    if (k >= 0) {
-      const unsigned long long t0 = global_ns();
-      unsigned polls = 0;
-      while (ld_acquire_gpu(a.tickets) < static_cast<unsigned>(a.n_splits)) {
-        if (++polls > kCombineMaxPolls || global_ns() - t0 > kCombineWaitNs) {
-          atomicOr(a.status, kDevCombineTimeout);
-          break;
-        }
-        __nanosleep(32);
-      }
-    }
-  }
-  if (k < 0) return;
-  __syncthreads();
-  for (int sl = k; sl < n_slices; sl += n_comb) {
-    if (a.xworld == 0) {
-      combine_slice(a.part_acc, a.part_ml, a.n_splits, a.qh, D, sl / kChunks, sl % kChunks,
-                    a.out, a.lse);
-    } else {
-      float o = 0.f, l2 = -INFINITY;
-      combine_slice_result(a.part_acc, a.part_ml, a.n_splits, a.qh, D, sl / kChunks,
-                           sl % kChunks, &o, &l2);
-      if (threadIdx.x < 32) exchange_slice<D>(a, epoch, sl, n_slices, o, l2);
-    }
-  }
-  if (threadIdx.x == 0) {
-    if (atomicAdd(a.tickets + 1, 1u) == static_cast<unsigned>(n_comb) - 1) {
-      atomicExch(a.tickets, 0u);
-      atomicExch(a.tickets + 1, 0u);
-      // every CTA read the epoch at its start, before its arrival: publish the completed call
-      if (a.xworld) *reinterpret_cast<volatile unsigned*>(a.xpeers[a.xrank]) = epoch;
-    }
-  }
-}
 
 template <int KVH, int GROUP>
 __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const DecodeArgs a) {
@@ -528,7 +383,7 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
               make_float2(acc[2 * j + k2][hh], acc[2 * j + k2][2 + hh]);
     }
   }
-  if (a.fuse_combine) fused_combine_tail<D>(a, epoch);
+  if (a.fuse_combine) fused_combine_tail<D>(a, epoch, a.n_splits);
 }
 
 using DecodeKernel = void (*)(const DecodeArgs);
