@@ -153,6 +153,24 @@ KVSSD_B200_API int kvssd_b200_decode_plan(int n_sel_blocks, int block_tokens, in
  * measurements and tests; AUTO restores the default. No reference counterpart. */
 KVSSD_B200_API int kvssd_b200_set_path_override(int path);
 
+/* Decodes n_records raw kvssd records already in device memory (record i at
+ * records + i * record_stride, the store's record_bytes) into PackedBatch tensors: packed_k /
+ * packed_v [n, bt, kvh, d*bits/8] u8, scales_k / scales_v [n, bt, kvh, d/group] FP16 bits,
+ * valid_tokens [n]. The header of each record (magic, version, geometry, payload length,
+ * optionally layer and block) is validated and the payload's zlib CRC-32 recomputed on the
+ * device; record_status[i] receives the OR of 1 = bad magic/version, 2 = geometry differs from
+ * the arguments, 4 = payload length differs, 8 = CRC mismatch, 16 = layer/block differs from
+ * `layer` (if >= 0) / expected_blocks[i] (if not NULL), 32 = valid count above block_tokens
+ * (clamped). Records with status bits 1, 2 or 4 are not copied and get valid 0. Replaces the
+ * CPU decode_record of the reference loader (src/kvssd/format.py:134-177,
+ * src/kvssd/loader.py:104-128), which checks the CRC on the host. */
+KVSSD_B200_API int kvssd_b200_decode_records(const uint8_t* records, size_t record_stride,
+                      int n_records, int layer, const int32_t* expected_blocks, int bits,
+                      int block_tokens, int kv_heads, int head_dim, int group_size,
+                      uint8_t* packed_k, uint8_t* packed_v, uint16_t* scales_k,
+                      uint16_t* scales_v, int32_t* valid_tokens, unsigned* record_status,
+                      kvssd_b200_stream_t stream);
+
 /* Size of a CUDA IPC memory handle (cudaIpcMemHandle_t). */
 #define KVSSD_B200_IPC_HANDLE_BYTES 64
 

@@ -16,6 +16,7 @@
 #include "../../include/kvssd_b200.h"
 #include "common.cuh"
 #include "decode.cuh"
+#include "records.cuh"
 
 namespace kvb {
 
@@ -642,6 +643,79 @@ int kvssd_b200_decode_exchange(const void* query, int query_dtype, const uint8_t
   if (st == KVSSD_B200_ERR_UNSUPPORTED)
     return fail(st, "the fused exchange needs a cooperative launch of the whole grid");
   return st;
+}
+
+int kvssd_b200_decode_records(const uint8_t* records, size_t record_stride, int n_records,
+                              int layer, const int32_t* expected_blocks, int bits,
+                              int block_tokens, int kv_heads, int head_dim, int group_size,
+                              uint8_t* packed_k, uint8_t* packed_v, uint16_t* scales_k,
+                              uint16_t* scales_v, int32_t* valid_tokens, unsigned* record_status,
+                              kvssd_b200_stream_t stream) {
+  if (n_records < 0) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "n_records must be >= 0");
+  if (n_records == 0) return KVSSD_B200_OK;
+  if (!records || !packed_k || !packed_v || !scales_k || !scales_v || !valid_tokens ||
+      !record_status)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "pointers must not be NULL");
+  if ((bits != 2 && bits != 4) || block_tokens < 1 || kv_heads < 1 || head_dim < 1 ||
+      group_size < 1 || head_dim % group_size || (head_dim * bits) % 8)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "bad cache geometry");
+  if ((reinterpret_cast<uintptr_t>(records) | record_stride) & 3u)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "records must be 4-byte aligned");
+  for (const void* p : {static_cast<const void*>(valid_tokens),
+                        static_cast<const void*>(record_status)})
+    if (reinterpret_cast<uintptr_t>(p) & 3u)
+      return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "valid_tokens/status must be 4-byte aligned");
+  const long long rows = static_cast<long long>(block_tokens) * kv_heads;
+  const long long scale_bytes = rows * (head_dim / group_size) * 2;
+  const long long packed_bytes = rows * (head_dim * bits / 8);
+  if (scale_bytes > (1LL << 30) || packed_bytes > (1LL << 30))
+    return fail(KVSSD_B200_ERR_UNSUPPORTED, "record sections above 1 GiB");
+  const long long payload = 2 * scale_bytes + 2 * packed_bytes;
+  if (static_cast<long long>(record_stride) < kRecHeaderBytes + payload)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "record stride smaller than header + payload");
+  RecordArgs a{};
+  a.records = records;
+  a.stride = record_stride;
+  a.n = n_records;
+  a.layer = layer;
+  a.blocks = expected_blocks;
+  a.bits = bits;
+  a.bt = block_tokens;
+  a.kvh = kv_heads;
+  a.d = head_dim;
+  a.group = group_size;
+  a.scale_bytes = static_cast<int>(scale_bytes);
+  a.packed_bytes = static_cast<int>(packed_bytes);
+  const bool out_aligned = ((reinterpret_cast<uintptr_t>(packed_k) | reinterpret_cast<uintptr_t>(packed_v) |
+                             reinterpret_cast<uintptr_t>(scales_k) | reinterpret_cast<uintptr_t>(scales_v)) & 3u) == 0;
+  // Word-granular copy and CRC when every section is whole 4-byte words (then the slices are
+  // too); slices: the largest power of two <= kRecThreads dividing the payload (in words or
+  // bytes). The tree folds need x^(8 * slice_bytes * 2^k) mod P, from x^8 by square-and-multiply.
+  a.words = (out_aligned && scale_bytes % 4 == 0 && packed_bytes % 4 == 0) ? 1 : 0;
+  const long long unit = a.words ? 4 : 1;
+  int slices = kRecThreads;
+  while (slices > 1 && payload % (unit * slices)) slices >>= 1;
+  a.slices = slices;
+  a.slice_bytes = static_cast<int>(payload / slices);
+  unsigned x8 = 1u << 31;  // x^0 in the reflected representation
+  for (int i = 0; i < 8; ++i) x8 = (x8 & 1u) ? (x8 >> 1) ^ 0xEDB88320u : x8 >> 1;
+  unsigned acc = 1u << 31, base = x8;
+  for (unsigned e = static_cast<unsigned>(a.slice_bytes); e; e >>= 1) {
+    if (e & 1u) acc = crc_mulmod(acc, base);
+    base = crc_mulmod(base, base);
+  }
+  for (int k = 0; k < kRecMaxLevels; ++k) {
+    a.shift[k] = acc;
+    acc = crc_mulmod(acc, acc);
+  }
+  a.packed_k = packed_k;
+  a.packed_v = packed_v;
+  a.scales_k = reinterpret_cast<uint8_t*>(scales_k);
+  a.scales_v = reinterpret_cast<uint8_t*>(scales_v);
+  a.valid = valid_tokens;
+  a.status = record_status;
+  cudaError_t e = launch_record_decode(a, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "record decode launch");
 }
 
 int kvssd_b200_read_status(void* workspace, int clear, unsigned* device_status,

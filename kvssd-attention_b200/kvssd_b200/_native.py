@@ -75,6 +75,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "kvssd_b200_set_path_override": (_c_int, [_c_int]),
     "kvssd_b200_read_status": (_c_int, [_c_void, _c_int, _c_uint_p, _c_void]),
+    "kvssd_b200_decode_records": (
+        _c_int,
+        [_c_void, _c_size, _c_int, _c_int, _c_void, _c_int, _c_int, _c_int, _c_int, _c_int,
+         _c_void, _c_void, _c_void, _c_void, _c_void, _c_void, _c_void],
+    ),
     "kvssd_b200_exchange_bytes": (_c_int, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_size)]),
     "kvssd_b200_exchange_alloc": (_c_int, [_c_size, ctypes.POINTER(_c_void)]),
     "kvssd_b200_exchange_clear": (_c_int, [_c_void, _c_size]),

@@ -198,6 +198,51 @@ def decode_exchange(query, packed_k, packed_v, scales_k, scales_v, valid_tokens,
     return out, lse
 
 
+RECORD_BAD_HEADER, RECORD_BAD_GEOMETRY, RECORD_BAD_LENGTH, RECORD_BAD_CRC = 1, 2, 4, 8
+RECORD_BAD_ID, RECORD_BAD_VALID = 16, 32
+
+
+def decode_records(records: torch.Tensor, spec, layer: int | None = None,
+                   block_ids: torch.Tensor | None = None):
+    """Raw kvssd records on a CUDA device -> PackedBatch tensors, CRC-32 checked on the device.
+
+    ``records`` is uint8 [n, record_bytes] (or flat, n * record_bytes), as read from the store.
+    Returns (packed_k, packed_v, scales_k, scales_v, valid_tokens, status) where status is
+    int32 [n] with the RECORD_BAD_* bits of each record (0 = good); see
+    kvssd_b200_decode_records. Asynchronous on the current stream.
+    """
+    device = records.device
+    if device.type != "cuda":
+        raise RuntimeError(f"decode_records requires a CUDA tensor, got {device}")
+    if records.dtype != torch.uint8 or not records.is_contiguous():
+        raise ValueError("records must be a contiguous uint8 tensor")
+    stride = spec.record_bytes
+    if records.numel() % stride:
+        raise ValueError(f"records must be whole records of {stride} bytes")
+    n = records.numel() // stride
+    bt, kvh = spec.block_tokens, spec.kv_heads
+    packed_k = torch.empty((n, bt, kvh, spec.packed_dim), dtype=torch.uint8, device=device)
+    packed_v = torch.empty_like(packed_k)
+    scales_k = torch.empty((n, bt, kvh, spec.groups), dtype=torch.float16, device=device)
+    scales_v = torch.empty_like(scales_k)
+    valid = torch.empty((n,), dtype=torch.int32, device=device)
+    status = torch.empty((n,), dtype=torch.int32, device=device)
+    if block_ids is not None:
+        block_ids = block_ids.to(device=device, dtype=torch.int32).contiguous()
+        if block_ids.shape != (n,):
+            raise ValueError("block_ids must name one block per record")
+    with torch.cuda.device(device):
+        _native.check(
+            _native.library().kvssd_b200_decode_records(
+                _ptr(records), stride, n, -1 if layer is None else int(layer), _ptr(block_ids),
+                spec.bits, bt, kvh, spec.head_dim, spec.group_size, _ptr(packed_k),
+                _ptr(packed_v), _ptr(scales_k), _ptr(scales_v), _ptr(valid), _ptr(status),
+                _stream_handle(device)),
+            "kvssd_b200_decode_records",
+        )
+    return packed_k, packed_v, scales_k, scales_v, valid, status
+
+
 def decode_split(query, packed_k, packed_v, scales_k, scales_v, valid_tokens, bits: int,
                  group_size: int, sm_scale: float, block_table=None) -> tuple[int, torch.Tensor]:
     """Runs only the streaming split-KV kernel; returns (n_parts, workspace).

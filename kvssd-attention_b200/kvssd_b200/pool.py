@@ -76,8 +76,35 @@ class DeviceBlockPool:
     @classmethod
     def from_store(cls, store, layer: int, device: torch.device | str,
                    verify_crc: bool = True) -> "DeviceBlockPool":
-        blocks = [store.read(layer, b, verify_crc) for b in store.blocks_for_layer(layer)]
-        return cls.from_blocks(store.spec, blocks, device)
+        """Loads every block of ``layer``: the raw records are read into one pinned buffer,
+        copied to the device in one transfer and decoded there (header checks and the payload
+        CRC-32 on the GPU, ops.decode_records). Raises like kvssd's decode_record on a bad
+        record: ValueError for a bad header or layout, IOError for a CRC mismatch."""
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise RuntimeError(f"DeviceBlockPool needs a CUDA device, got {device}")
+        spec = store.spec
+        ids = store.blocks_for_layer(layer)
+        if not ids:
+            raise ValueError(f"layer {layer} has no blocks")
+        raw = torch.empty((len(ids), spec.record_bytes), dtype=torch.uint8,
+                          pin_memory=torch.cuda.is_available())
+        for i, b in enumerate(ids):
+            store.read_into(store.entry(layer, b), raw[i])
+        dev = raw.to(device, non_blocking=True)
+        kp, vp, ks, vs, valid, status = ops.decode_records(
+            dev, spec, layer, torch.tensor(ids, dtype=torch.int32))
+        bad = status.cpu()
+        if verify_crc is False:
+            bad &= ~ops.RECORD_BAD_CRC
+        for i, st in enumerate(bad.tolist()):
+            if st & (ops.RECORD_BAD_HEADER | ops.RECORD_BAD_ID):
+                raise ValueError(f"invalid KVSSD record header (layer={layer}, block={ids[i]})")
+            if st & (ops.RECORD_BAD_GEOMETRY | ops.RECORD_BAD_LENGTH):
+                raise ValueError("record layout does not match manifest")
+            if st & ops.RECORD_BAD_CRC:
+                raise IOError(f"CRC mismatch for layer={layer}, block={ids[i]}")
+        return cls(spec, kp, vp, ks, vs, valid, ids)
 
     @property
     def n_blocks(self) -> int:
