@@ -24,6 +24,7 @@ import io
 import json
 import math
 import os
+import shutil
 import statistics
 import subprocess
 import sys
@@ -52,6 +53,8 @@ def parse_args():
     ap.add_argument("--copies", type=int, default=3,
                     help="input copies rotated between steps so no step reads from L2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-pipeline", action="store_true",
+                    help="skip the KVSSDPipeline and record-decode legs")
     ap.add_argument("--path", choices=["auto", "stream", "regs", "generic"], default="auto",
                     help="A/B: force the cp.async-streamed, register-fed or CUDA-core decode kernel")
     ap.add_argument("--eager", action="store_true",
@@ -197,6 +200,67 @@ def run_reference(args) -> None:
                                    "host)"},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     })
+
+
+def pipeline_legs(w, base, q, scale, device, rank, args) -> dict:
+    """Times KVSSDPipeline.decode end to end from a store file of the layer, and the on-GPU
+    record decode alone on the layer's records in HBM."""
+    from kvssd_b200 import CacheSpec, KVCacheStore, KVSSDPipeline, ops
+    from kvssd_b200.format import PackedKVBlock
+    from kvssd_b200.quant import QuantizedTensor
+
+    spec = CacheSpec(1, w.kv_heads, w.head_dim, w.block_tokens, w.bits, w.group_size)
+    shape = (w.block_tokens, w.kv_heads, w.head_dim)
+    kp, vp = base.packed_k.cpu(), base.packed_v.cpu()
+    ks, vs, valid = base.scales_k.cpu(), base.scales_v.cpu(), base.valid_tokens.cpu()
+    blocks = (PackedKVBlock(0, b, int(valid[b]),
+                            QuantizedTensor(kp[b], ks[b], shape, w.bits, w.group_size),
+                            QuantizedTensor(vp[b], vs[b], shape, w.bits, w.group_size))
+              for b in range(kp.shape[0]))
+    root = Path(tempfile.mkdtemp(prefix=f"kvssd_bench_r{rank}_", dir="/dev/shm"
+                                 if Path("/dev/shm").is_dir() else None))
+    store = KVCacheStore.from_blocks(root, spec, blocks)
+    record_bytes = kp.shape[0] * spec.record_bytes
+    try:
+        pipe = KVSSDPipeline(store, device=device, io_depth=8, stage_blocks=128,
+                             require_cuda_kernel=True)
+        qh = q.float()
+        for _ in range(2):
+            pipe.decode(qh, 0)
+        torch.cuda.synchronize(device)
+        steps = max(2, min(args.steps, 5))
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            out = pipe.decode(qh, 0)
+            out.cpu()
+        pipe_s = (time.perf_counter() - t0) / steps
+        raw = store.read_records(0, store.blocks_for_layer(0)).to(device)
+        for _ in range(3):
+            ops.decode_records(raw, spec, 0)
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            ops.decode_records(raw, spec, 0)
+        e1.record()
+        torch.cuda.synchronize(device)
+        rec_ms = e0.elapsed_time(e1) / 10
+        pipe.close()
+    finally:
+        store.close()
+        shutil.rmtree(root, ignore_errors=True)
+    nbytes = w.blocks_per_layer * w.bytes_per_block
+    return {
+        "KVSSDPipeline_decode": {
+            "value": nbytes / pipe_s / 1e9, "unit": "GB/s", "ms_per_step": pipe_s * 1e3,
+            "path": "KVSSDPipeline(store, stage_blocks=128, io_depth=8).decode(query, 0): "
+                    "store file in /dev/shm (page cache), native record reads, H2D, on-GPU "
+                    "record decode with CRC-32, fused decode, chunk merge; host wall clock"},
+        "record_decode_on_gpu": {
+            "value": record_bytes / (rec_ms * 1e-3) / 1e9, "unit": "GB/s of records",
+            "us_per_layer": rec_ms * 1e3,
+            "note": "1024 raw records resident in HBM -> PackedBatch + CRC-32 check"},
+    }
 
 
 def run_ours(args) -> None:
@@ -381,6 +445,14 @@ def run_ours(args) -> None:
     e2e_ms = timed(e2e_step, e2e_steps, 3)
     e2e_value = world * nbytes / (e2e_ms * 1e-3) / 1e9
 
+    # ---- the reference's own entry point, KVSSDPipeline.decode(query, layer), from a store file
+    # of this rank's layer: native record reads (page cache), chunked host-to-device copies,
+    # on-GPU record decode (headers + CRC-32) and the fused decode; plus the GPU record decode
+    # alone on the layer's records resident in HBM.
+    pipeline = None
+    if not args.no_pipeline and world == 1:
+        pipeline = pipeline_legs(w, base, q, scale, device, rank, args)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_oracle_run(args.cpu_seconds)
@@ -437,6 +509,8 @@ def run_ours(args) -> None:
     }
     if cpu is not None:
         record["cpu_baseline"] = cpu
+    if pipeline is not None:
+        record["pipeline"] = pipeline
     emit(record)
 
 

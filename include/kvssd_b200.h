@@ -171,6 +171,20 @@ KVSSD_B200_API int kvssd_b200_decode_records(const uint8_t* records, size_t reco
                       uint16_t* scales_v, int32_t* valid_tokens, unsigned* record_status,
                       kvssd_b200_stream_t stream);
 
+/* Reads n_records whole records (record_bytes each, at the given byte offsets of the store
+ * file `path`) into `destination` (n_records * record_bytes bytes, record i at
+ * i * record_bytes) with `threads` reader threads. With `direct` nonzero and 4 KiB-aligned
+ * offsets, sizes and destination the file is opened with O_DIRECT (page cache bypassed), else
+ * (or where the file system refuses O_DIRECT) with buffered pread; *used_direct (if not NULL)
+ * tells which. Host-only: a pinned buffer here feeds kvssd_b200_decode_records after one
+ * host-to-device copy. Replaces the reference's storage backends' record reads
+ * (src/kvssd/storage/direct.py:64-88, buffered.py:53-76) for whole-record batches. On error
+ * kvssd_b200_io_last_error describes it. */
+KVSSD_B200_API int kvssd_b200_read_records(const char* path, const long long* offsets,
+                                           int n_records, size_t record_bytes, void* destination,
+                                           int threads, int direct, int* used_direct);
+KVSSD_B200_API const char* kvssd_b200_io_last_error(void);
+
 /* Size of a CUDA IPC memory handle (cudaIpcMemHandle_t). */
 #define KVSSD_B200_IPC_HANDLE_BYTES 64
 

@@ -2,7 +2,7 @@
 
 The library is a plain C-ABI shared object (no torch headers, no Python extension module):
 ``python -m kvssd_b200._build`` or ``kvssd_b200._build.build()`` compiles every ``csrc/*.cu``
-into ``kvssd_b200/lib/libkvssd_b200.so``. Objects are rebuilt only when a source or header
+and ``csrc/*.cpp`` (host-only code) into ``kvssd_b200/lib/libkvssd_b200.so``. Objects are rebuilt only when a source or header
 is newer than the library.
 """
 
@@ -49,7 +49,7 @@ def _nvcc() -> str:
 
 
 def _sources() -> list[Path]:
-    return sorted(CSRC_DIR.glob("*.cu"))
+    return sorted(CSRC_DIR.glob("*.cu")) + sorted(CSRC_DIR.glob("*.cpp"))
 
 
 def _headers() -> list[Path]:
@@ -75,7 +75,8 @@ def build(verbose: bool = False, force: bool = False) -> Path:
         obj = BUILD_DIR / (src.stem + ".o")
         objects.append(obj)
         if force or _stale(obj, [src, *headers]):
-            cmd = [nvcc, *NVCC_FLAGS, "-I", str(INCLUDE_DIR), "-c", str(src), "-o", str(obj)]
+            extra = ["-Xcompiler", "-pthread"] if src.suffix == ".cpp" else []
+            cmd = [nvcc, *NVCC_FLAGS, *extra, "-I", str(INCLUDE_DIR), "-c", str(src), "-o", str(obj)]
             jobs.append(cmd)
 
     def run(cmd: list[str]) -> None:
@@ -89,7 +90,7 @@ def build(verbose: bool = False, force: bool = False) -> Path:
         list(pool.map(run, jobs))
     if force or jobs or _stale(LIB_PATH, objects):
         tmp = LIB_PATH.with_suffix(".so.tmp")
-        run([nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *map(str, objects)])
+        run([nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *map(str, objects), "-lpthread"])
         os.replace(tmp, LIB_PATH)
     return LIB_PATH
 

@@ -1,11 +1,16 @@
-"""KVSSDPipeline: selection -> record reads -> staging -> fused decode -> exact merge.
+"""KVSSDPipeline: selection -> record reads -> on-GPU record decode -> fused decode -> exact merge.
 
 API of src/kvssd/pipeline.py:19-196 (constructor arguments, ``decode(query, layer,
-selector)``, context manager). Execution is CUDA-only: records are read by the bounded
-loader, copied chunk by chunk (``stage_blocks`` blocks) into reusable pinned buffers, sent to
-the device on a transfer stream, and each chunk is decoded on a compute stream as soon as
-its copy lands; the per-chunk (out, lse) pairs are merged exactly by one N-way merge kernel
-at the end (the reference chains one pairwise merge per chunk). For a layer that stays
+selector)``, context manager). Execution is CUDA-only. The selected records are read chunk by
+chunk (``stage_blocks`` records) by the native reader (``io_depth`` threads, O_DIRECT where
+the file system allows it) into two reusable pinned buffers; each chunk is copied to the device
+on a transfer stream as one transfer, and on a compute stream, as soon as its copy lands, the
+records are decoded into PackedBatch tensors with their headers and payload CRC-32 checked on
+the GPU (ops.decode_records) and attended by the fused decode kernel. Reading chunk i + 1 on
+the host overlaps the GPU work of chunk i. The per-chunk (out, lse) pairs are merged exactly
+by one N-way merge kernel (the reference chains one pairwise merge per chunk), and the records'
+integrity statuses are read back once at the end: a bad record raises as kvssd's decode_record
+does (ValueError for a bad header or layout, IOError for a CRC mismatch). For a layer that stays
 resident in HBM use DeviceBlockPool, which decodes with a single launch.
 """
 
@@ -17,27 +22,20 @@ import torch
 
 from . import ops
 from .backends import AttentionBackend, resolve_attention_backend
-from .loader import AsyncBlockLoader
 from .selectors import AllBlocks, BlockSelector
 
 
 class _PinnedChunk:
-    """Stacked pinned host tensors for one chunk of blocks plus its copy-done event."""
+    """Pinned raw records of one chunk plus the event of its last host-to-device copy."""
 
     def __init__(self, spec, blocks: int):
-        pin = torch.cuda.is_available()
-        p = (blocks, spec.block_tokens, spec.kv_heads, spec.packed_dim)
-        s = (blocks, spec.block_tokens, spec.kv_heads, spec.groups)
-        self.kp = torch.empty(p, dtype=torch.uint8, pin_memory=pin)
-        self.vp = torch.empty(p, dtype=torch.uint8, pin_memory=pin)
-        self.ks = torch.empty(s, dtype=torch.float16, pin_memory=pin)
-        self.vs = torch.empty(s, dtype=torch.float16, pin_memory=pin)
-        self.valid = torch.empty(blocks, dtype=torch.int32, pin_memory=pin)
+        self.raw = torch.empty((blocks, spec.record_bytes), dtype=torch.uint8,
+                               pin_memory=torch.cuda.is_available())
         self.copied: torch.cuda.Event | None = None
 
 
 class KVSSDPipeline:
-    """End-to-end selection, prefetch, pinned staging and fused packed attention."""
+    """End-to-end selection, native record reads, on-GPU record decode and fused attention."""
 
     def __init__(
         self,
@@ -52,27 +50,20 @@ class KVSSDPipeline:
         self.device = torch.device(device)
         if self.device.type == "cuda" and not torch.cuda.is_available():
             raise RuntimeError("CUDA device requested but CUDA is unavailable")
+        if io_depth < 1:
+            raise ValueError("io_depth must be positive")
         if stage_blocks < 1:
             raise ValueError("stage_blocks must be positive")
         if require_cuda_kernel and attention_backend not in (None, "auto", "cuda"):
             raise ValueError("require_cuda_kernel conflicts with a non-CUDA attention backend")
         requested = "cuda" if require_cuda_kernel else attention_backend
         self.attention_backend = resolve_attention_backend(requested, self.device)
-        self.loader = AsyncBlockLoader(store, depth=io_depth, pinned=True)
+        self.io_depth = io_depth
         self.stage_blocks = stage_blocks
         self.require_cuda_kernel = require_cuda_kernel
         self.transfer_stream = torch.cuda.Stream(device=self.device)
         self.compute_stream = torch.cuda.Stream(device=self.device)
         self._ring = [_PinnedChunk(store.spec, stage_blocks) for _ in range(2)]
-
-    def _stage(self, chunk: _PinnedChunk, count: int) -> tuple[torch.Tensor, ...]:
-        """Enqueues the H2D copy of the first ``count`` blocks of a pinned chunk."""
-        with torch.cuda.stream(self.transfer_stream):
-            dev = tuple(t[:count].to(self.device, non_blocking=True)
-                        for t in (chunk.kp, chunk.vp, chunk.ks, chunk.vs, chunk.valid))
-            chunk.copied = torch.cuda.Event()
-            chunk.copied.record(self.transfer_stream)
-        return dev
 
     def decode(self, query: torch.Tensor, layer: int,
                selector: BlockSelector | None = None) -> torch.Tensor:
@@ -90,36 +81,28 @@ class KVSSDPipeline:
         with torch.cuda.stream(self.compute_stream):
             outs = torch.empty((n_chunks, qh, d), dtype=torch.float32, device=self.device)
             lses = torch.empty((n_chunks, qh), dtype=torch.float32, device=self.device)
+            statuses = torch.empty((len(selected),), dtype=torch.int32, device=self.device)
+            ids = torch.tensor(selected, dtype=torch.int32).to(self.device, non_blocking=True)
         query.record_stream(self.compute_stream)
 
-        def launch(dev: tuple[torch.Tensor, ...], ready: torch.cuda.Event, index: int) -> None:
-            with torch.cuda.stream(self.compute_stream):
-                self.compute_stream.wait_event(ready)
-                ops.decode(query, dev[0], dev[1], dev[2], dev[3], dev[4], spec.bits,
-                           spec.group_size, scale, out=outs[index], lse=lses[index])
-                for t in dev:
-                    t.record_stream(self.compute_stream)
-
-        filled = 0
-        index = 0
-        chunk = self._ring[0]
-        for block in self.loader.iter_records(layer, selected):
-            if filled == 0 and chunk.copied is not None:
+        for ci in range(n_chunks):
+            lo, hi = ci * self.stage_blocks, min(len(selected), (ci + 1) * self.stage_blocks)
+            chunk = self._ring[ci % len(self._ring)]
+            if chunk.copied is not None:
                 chunk.copied.synchronize()  # the pinned buffer's previous copy has landed
-            chunk.kp[filled].copy_(block.key.packed)
-            chunk.vp[filled].copy_(block.value.packed)
-            chunk.ks[filled].copy_(block.key.scales)
-            chunk.vs[filled].copy_(block.value.scales)
-            chunk.valid[filled] = block.valid_tokens
-            filled += 1
-            if filled == self.stage_blocks:
-                launch(self._stage(chunk, filled), chunk.copied, index)
-                index += 1
-                filled = 0
-                chunk = self._ring[index % len(self._ring)]
-        if filled:
-            launch(self._stage(chunk, filled), chunk.copied, index)
-            index += 1
+            raw = self.store.read_records(layer, selected[lo:hi], destination=chunk.raw,
+                                          threads=self.io_depth)
+            with torch.cuda.stream(self.transfer_stream):
+                dev = raw.to(self.device, non_blocking=True)
+                chunk.copied = torch.cuda.Event()
+                chunk.copied.record(self.transfer_stream)
+            with torch.cuda.stream(self.compute_stream):
+                self.compute_stream.wait_event(chunk.copied)
+                kp, vp, ks, vs, valid, status = ops.decode_records(dev, spec, layer, ids[lo:hi])
+                ops.decode(query, kp, vp, ks, vs, valid, spec.bits, spec.group_size, scale,
+                           out=outs[ci], lse=lses[ci])
+                statuses[lo:hi].copy_(status)
+                dev.record_stream(self.compute_stream)
         with torch.cuda.stream(self.compute_stream):
             if n_chunks == 1:
                 out = outs[0]
@@ -129,10 +112,25 @@ class KVSSDPipeline:
         done.record(self.compute_stream)
         caller.wait_event(done)
         out.record_stream(caller)
+        self._raise_on_bad_records(statuses, selected, layer)
         return out.to(query.dtype)
 
+    @staticmethod
+    def _raise_on_bad_records(statuses: torch.Tensor, selected: list[int], layer: int) -> None:
+        bad = statuses.cpu()  # waits for the chunks' record decodes
+        if not torch.any(bad):
+            return
+        for i, st in enumerate(bad.tolist()):
+            if st & (ops.RECORD_BAD_HEADER | ops.RECORD_BAD_ID):
+                raise ValueError(f"invalid KVSSD record header (layer={layer}, "
+                                 f"block={selected[i]})")
+            if st & (ops.RECORD_BAD_GEOMETRY | ops.RECORD_BAD_LENGTH):
+                raise ValueError("record layout does not match manifest")
+            if st & ops.RECORD_BAD_CRC:
+                raise IOError(f"CRC mismatch for layer={layer}, block={selected[i]}")
+
     def close(self) -> None:
-        self.loader.close()
+        torch.cuda.synchronize(self.device)
 
     def __enter__(self) -> "KVSSDPipeline":
         return self

@@ -120,6 +120,25 @@ class KVCacheStore:
         return cls(root, manifest, storage_backend)
 
     @classmethod
+    def from_blocks(cls, root: str | Path, spec: CacheSpec, blocks) -> "KVCacheStore":
+        """Writes already-quantized PackedKVBlocks (any order of (layer, block)) as a store in
+        the same byte format as ``create``."""
+        spec.validate()
+        root = Path(root)
+        root.mkdir(parents=True, exist_ok=True)
+        entries: list[BlockEntry] = []
+        with (root / DATA_FILE).open("wb") as out:
+            for block in blocks:
+                record, crc = encode_record(block, spec)
+                offset = out.tell()
+                out.write(record)
+                entries.append(BlockEntry(block.layer, block.block, offset, len(record),
+                                          block.valid_tokens, crc))
+        manifest = Manifest(spec=spec, entries=entries)
+        manifest.save(root / MANIFEST_FILE)
+        return cls(root, manifest)
+
+    @classmethod
     def open(cls, root: str | Path, storage_backend: str | None = None) -> "KVCacheStore":
         root = Path(root)
         manifest = Manifest.load(root / MANIFEST_FILE)
@@ -138,6 +157,42 @@ class KVCacheStore:
 
     def read_into(self, entry: BlockEntry, destination: torch.Tensor) -> None:
         self._file.read_into(entry, destination)
+
+    def read_records(self, layer: int, block_ids, destination: torch.Tensor | None = None,
+                     threads: int = 8, direct: bool = True) -> torch.Tensor:
+        """Raw records of ``block_ids`` in one call of the native reader (O_DIRECT where the file
+        system allows it, a pool of reader threads). Returns uint8 [n, record_bytes] (pinned
+        when CUDA is available, or ``destination``), ready for one host-to-device copy and
+        ops.decode_records on the GPU."""
+        import ctypes
+
+        from . import _native
+
+        ids = list(block_ids)
+        rb = self.spec.record_bytes
+        if destination is None:
+            destination = torch.empty((len(ids), rb), dtype=torch.uint8,
+                                      pin_memory=torch.cuda.is_available())
+        if destination.dtype != torch.uint8 or destination.device.type != "cpu" or \
+                not destination.is_contiguous() or destination.numel() < len(ids) * rb:
+            raise ValueError("destination must be a contiguous CPU uint8 tensor of n records")
+        if not ids:
+            return destination[:0]
+        offsets = (ctypes.c_longlong * len(ids))()
+        for i, b in enumerate(ids):
+            entry = self.entry(layer, b)
+            if entry.length != rb:
+                raise ValueError("records of one store all have the spec's record_bytes")
+            offsets[i] = entry.offset
+        used = ctypes.c_int()
+        lib = _native.library()
+        status = lib.kvssd_b200_read_records(str(self._file.path).encode(), offsets, len(ids), rb,
+                                             destination.data_ptr(), threads, int(direct),
+                                             ctypes.byref(used))
+        if status != _native.OK:
+            raise OSError(f"record read failed: {lib.kvssd_b200_io_last_error().decode()}")
+        self.last_read_direct = bool(used.value)
+        return destination[: len(ids)].view(len(ids), rb)
 
     def read(self, layer: int, block: int, verify_crc: bool = True) -> PackedKVBlock:
         entry = self.entry(layer, block)

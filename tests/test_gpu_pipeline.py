@@ -81,6 +81,25 @@ def test_pipeline_selection_and_chunking(tmp_path: Path, stage_blocks, selector)
     store.close()
 
 
+def test_pipeline_detects_corrupt_record_on_device(tmp_path: Path):
+    store = _store(tmp_path, tokens=200)
+    q = torch.randn(32, 128, generator=torch.Generator().manual_seed(3)).half()
+    entry = store.entry(0, 5)
+    store.close()
+    path = tmp_path / "blocks.kvssd"
+    data = bytearray(path.read_bytes())
+    data[entry.offset + 52 + 1000] ^= 0x10  # one payload bit: only the CRC can tell
+    path.write_bytes(bytes(data))
+    store = KVCacheStore.open(tmp_path)
+    with KVSSDPipeline(store, device=DEV, stage_blocks=4) as pipe:
+        with pytest.raises(IOError, match="CRC mismatch for layer=0, block=5"):
+            pipe.decode(q, 0)
+        out = pipe.decode(q, 0, RecentSinkBlocks(2, 3))  # block 5 not selected: fine
+        torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    store.close()
+
+
 def test_pipeline_rejects_empty_selection(tmp_path: Path):
     store = _store(tmp_path, tokens=64)
     with KVSSDPipeline(store, device=DEV) as pipe:

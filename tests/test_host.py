@@ -239,3 +239,23 @@ def test_workload_geometry():
     assert c3.bytes_per_block * len(c3.selected_blocks()) == 2703360
     assert WORKLOADS["c5"].bytes_per_block * WORKLOADS["c5"].blocks_per_layer == 1207959552
     assert f16(np.array([0x3C00], np.uint16))[0] == 1.0
+
+
+def test_native_record_reader_matches_pread(tmp_path: Path):
+    shutil.copytree(GOLDEN / "store_small", tmp_path / "s")
+    store = KVCacheStore.open(tmp_path / "s")
+    for layer in range(store.spec.layers):
+        ids = store.blocks_for_layer(layer)
+        for direct in (True, False):
+            raw = store.read_records(layer, list(reversed(ids)), threads=3, direct=direct)
+            for i, b in enumerate(reversed(ids)):
+                ref = torch.empty(store.spec.record_bytes, dtype=torch.uint8)
+                store.read_into(store.entry(layer, b), ref)
+                assert torch.equal(raw[i], ref)
+    # a record past the end of the file is an error, not a short buffer
+    entry = store.entry(0, store.blocks_for_layer(0)[-1])
+    (tmp_path / "s" / "blocks.kvssd").write_bytes(
+        (tmp_path / "s" / "blocks.kvssd").read_bytes()[: entry.offset + 100])
+    store2 = KVCacheStore.open(tmp_path / "s")
+    with pytest.raises(OSError, match="short read"):
+        store2.read_records(0, [store.blocks_for_layer(0)[-1]])
