@@ -263,6 +263,62 @@ def pipeline_legs(w, base, q, scale, device, rank, args) -> dict:
     }
 
 
+def c4_legs(w, base, device, args) -> dict:
+    """The multi-layer step of c4 on one GPU: 32 layers x 65536 tokens (each layer 512 blocks of
+    distinct memory: halves of 16 copies of this workload's pool), each with its own query,
+    decoded by one batched launch and by 32 single decodes; CUDA-graph replays, device time."""
+    from kvssd_b200 import ops
+
+    layers, per = 32, w.blocks_per_layer // 2
+    copies = [[t.clone() for t in (base.packed_k, base.packed_v, base.scales_k, base.scales_v,
+                                   base.valid_tokens)] for _ in range(layers // 2)]
+    pools = [[t[h * per:(h + 1) * per] for t in copies[i // 2]] for i, h in
+             ((i, i % 2) for i in range(layers))]
+    gen = torch.Generator().manual_seed(4)
+    queries = [torch.randn(w.query_heads, w.head_dim, generator=gen).half().to(device)
+               for _ in range(layers)]
+    problems = [(q, *p, None) for q, p in zip(queries, pools)]
+    scale = 1 / math.sqrt(w.head_dim)
+    stream = torch.cuda.current_stream(device)
+
+    def graph_time(fn, reps: int = 20) -> float:
+        for _ in range(3):
+            fn()
+        side = torch.cuda.Stream(device)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize(device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for _ in range(reps):
+                fn()
+        g.replay()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        del g
+        return e0.elapsed_time(e1) / reps
+
+    batch = ops.BatchedDecode(problems, w.bits, w.group_size, scale)
+    batched_ms = graph_time(batch.run)
+    single_ms = graph_time(lambda: [ops.decode(q, *p, w.bits, w.group_size, scale)
+                                    for q, p in zip(queries, pools)])
+    step_bytes = layers * per * w.bytes_per_block
+    return {
+        "workload": "c4 on 1 GPU: 32 layers x 65536 tokens, INT4 g32, 8 KV heads, GQA 4",
+        "batched_one_launch": {"us_per_layer": batched_ms * 1e3 / layers,
+                               "GB/s": step_bytes / (batched_ms * 1e-3) / 1e9},
+        "one_decode_per_layer": {"us_per_layer": single_ms * 1e3 / layers,
+                                 "GB/s": step_bytes / (single_ms * 1e-3) / 1e9},
+        "bytes_per_step": step_bytes,
+    }
+
+
 def run_ours(args) -> None:
     from kvssd_b200 import B200AttentionBackend, PackedBatch, ops
     from kvssd_b200.sharding import ShardedDecoder
@@ -450,8 +506,10 @@ def run_ours(args) -> None:
     # on-GPU record decode (headers + CRC-32) and the fused decode; plus the GPU record decode
     # alone on the layer's records resident in HBM.
     pipeline = None
+    c4 = None
     if not args.no_pipeline and world == 1:
         pipeline = pipeline_legs(w, base, q, scale, device, rank, args)
+        c4 = c4_legs(w, base, device, args)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -511,6 +569,8 @@ def run_ours(args) -> None:
         record["cpu_baseline"] = cpu
     if pipeline is not None:
         record["pipeline"] = pipeline
+    if c4 is not None:
+        record["c4_multi_layer"] = c4
     emit(record)
 
 

@@ -84,7 +84,7 @@ KVSSD_B200_API int kvssd_b200_decode_workspace_size(int n_sel_blocks, int block_
  * valid_tokens entries are never dereferenced: they are skipped/clamped and recorded in the
  * workspace status word (see kvssd_b200_read_status). Outputs: out, lse as in the header.
  * The workspace (>= kvssd_b200_decode_workspace_size bytes, 16-byte aligned) starts with a
- * 256-byte header holding that sticky status word and the arrival counters of the fused
+ * 2048-byte header holding that sticky status word and the arrival counters of the fused
  * combine (the streaming kernel folds its split-KV parts itself; the counters return to zero
  * at the end of every call): zero the header once after allocating the workspace. Calls
  * sharing one workspace must be ordered on the GPU (same stream or explicit events). */
@@ -106,10 +106,10 @@ KVSSD_B200_API int kvssd_b200_decode(const void* query, int query_dtype, const u
  * For callers that cannot allocate device memory on the decode path: hosts that bind the C ABI
  * without a device allocator of their own (a plain C, cgo or JNI host), and serving loops
  * that must not call cudaMalloc/cudaFree there, which synchronise the device.
- * Limits: a geometry whose plan needs more than KVSSD_B200_STATIC_SCRATCH_BYTES (256 bytes of
+ * Limits: a geometry whose plan needs more than KVSSD_B200_STATIC_SCRATCH_BYTES (2048 bytes of
  * header plus n_parts * query_heads * (head_dim + 2) * 4; the c2 shape needs 2.5 MB) is
  * rejected with KVSSD_B200_ERR_WORKSPACE before anything is launched. The first call on each
- * device resolves the scratch address and zeroes its 256-byte status header (the only part
+ * device resolves the scratch address and zeroes its 2048-byte header (the only part
  * that must start at zero) on `stream`; make that first call before any stream capture.
  * Every call on a device uses the same scratch, so calls on one device must not overlap in
  * time (one stream, or events between streams): overlapping calls race on the parts.
@@ -184,6 +184,43 @@ KVSSD_B200_API int kvssd_b200_read_records(const char* path, const long long* of
                                            int n_records, size_t record_bytes, void* destination,
                                            int threads, int direct, int* used_direct);
 KVSSD_B200_API const char* kvssd_b200_io_last_error(void);
+
+/* One problem of a batched decode: its query [query_heads, head_dim], block pool
+ * (PackedBatch layout), optional block table (NULL = all pool blocks in order) and outputs.
+ * Problems of one batch share the geometry; their pools may be shared (a batch of sequences
+ * over one paged pool) or separate (several layers). */
+typedef struct kvssd_b200_problem {
+  const void* query;
+  const uint8_t* packed_k;
+  const uint8_t* packed_v;
+  const uint16_t* scales_k;
+  const uint16_t* scales_v;
+  const int32_t* valid_tokens;
+  const int32_t* block_table;
+  float* out;
+  float* lse;
+  int n_pool_blocks;
+  int n_sel_blocks;
+} kvssd_b200_problem;
+
+/* Workspace bytes of kvssd_b200_decode_batched for n_problems problems. */
+KVSSD_B200_API int kvssd_b200_decode_batched_workspace_size(int n_problems, int block_tokens,
+                      int query_heads, int kv_heads, int head_dim, int bits, int group_size,
+                      size_t* bytes);
+
+/* n_problems independent decodes in ONE launch: `problems` is a DEVICE array of
+ * kvssd_b200_problem (so the call can be captured in a CUDA graph and replayed with new
+ * descriptor contents). The grid gets floor(SMs / n_problems) CTAs per problem (at least 1);
+ * each problem's split-KV parts are folded by its own CTAs in the grid's tail. Needs the
+ * streaming kernel's shapes (INT4, head_dim 128, group 32 or 64, 16-byte aligned operands)
+ * and n_problems <= the SM count; workspace as kvssd_b200_decode (zero its 2048-byte header
+ * once). Amortises the per-decode tail and launch over a multi-layer step or a batch of
+ * sequences (the reference decodes one layer per call, src/kvssd/pipeline.py:167-187). No
+ * reference counterpart. */
+KVSSD_B200_API int kvssd_b200_decode_batched(const kvssd_b200_problem* problems, int n_problems,
+                      int query_dtype, int block_tokens, int query_heads, int kv_heads,
+                      int head_dim, int bits, int group_size, float sm_scale, void* workspace,
+                      size_t workspace_bytes, kvssd_b200_stream_t stream);
 
 /* Size of a CUDA IPC memory handle (cudaIpcMemHandle_t). */
 #define KVSSD_B200_IPC_HANDLE_BYTES 64

@@ -23,7 +23,7 @@ namespace kvb {
 using DecodeKernel = void (*)(const DecodeArgs);
 DecodeKernel tc_decode_kernel_for(int bits, int d, int group);
 DecodeKernel simt_decode_kernel_for(int d);
-DecodeKernel async_decode_kernel_for(int bits, int d, int group, int kvh);
+DecodeKernel async_decode_kernel_for(int bits, int d, int group, int kvh, bool batched);
 int async_threads();
 int async_warps();
 int async_depth();
@@ -52,8 +52,12 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(KVSSD_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-constexpr size_t kHeaderBytes = 256;  // workspace header: device status word, counters, padding
-constexpr size_t kTicketOffset = 128;  // the fused combine's two arrival counters
+// Workspace header, zeroed once by the caller and zero again after every call: the device
+// status word (byte 0), the fused combine's two arrival counters (byte 128) and the batched
+// decode's two counters per problem (byte 256, up to 148 problems).
+constexpr size_t kHeaderBytes = 2048;
+constexpr size_t kTicketOffset = 128;
+constexpr size_t kProblemTicketOffset = 256;
 constexpr int kMaxParts = 8192;       // bound on split-KV parts
 
 struct DeviceInfo {
@@ -135,7 +139,7 @@ int choose_path(int d, int bits, int group) {
 // geometry does not qualify (INT4, head_dim 128, group 32 or 64, KV heads dividing the 16
 // warps, at most 8 query heads per KV head).
 bool plan_streaming(const Geometry& g, const DeviceInfo& info, Plan& p) {
-  p.kernel = async_decode_kernel_for(g.bits, g.d, g.group, g.kvh);
+  p.kernel = async_decode_kernel_for(g.bits, g.d, g.group, g.kvh, false);
   if (p.kernel == nullptr) return false;
   if (p.n_qsub != 1 || async_warps() % g.kvh) return false;
   p.smem = static_cast<size_t>(async_warps()) * async_depth() * async_stage_bytes(g.group);
@@ -716,6 +720,139 @@ int kvssd_b200_decode_records(const uint8_t* records, size_t record_stride, int 
   a.status = record_status;
   cudaError_t e = launch_record_decode(a, reinterpret_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "record decode launch");
+}
+
+}  // extern "C"
+
+namespace kvb {
+namespace {
+
+// Plan of a batched decode: the streaming kernel's geometry checks, CTAs per problem and the
+// workspace layout (header, 2 ticket words per problem, then the problems' parts).
+struct BatchPlan {
+  Plan p;
+  int ctas = 0;
+  size_t ws_bytes = 0;
+};
+
+int plan_batched(int n_problems, int block_tokens, int query_heads, int kv_heads, int head_dim,
+                 int bits, int group_size, BatchPlan& bp) {
+  if (n_problems < 1) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "n_problems must be >= 1");
+  const Geometry g{1, block_tokens, query_heads, kv_heads, head_dim, bits, group_size};
+  int st = check_geometry(g);
+  if (st) return st;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  const DeviceInfo info = device_info(dev);
+  if (n_problems > info.sms)
+    return fail(KVSSD_B200_ERR_UNSUPPORTED, "a batched decode takes at most one problem per SM");
+  Plan& p = bp.p;
+  p.gqa = query_heads / kv_heads;
+  p.n_qsub = (p.gqa + 7) / 8;
+  p.n_vheads = kv_heads * p.n_qsub;
+  if (!plan_streaming(g, info, p))
+    return fail(KVSSD_B200_ERR_UNSUPPORTED,
+                "batched decode needs the streaming kernel's shapes (INT4, head_dim 128, group "
+                "32 or 64, KV heads dividing 16, at most 8 query heads per KV head)");
+  p.kernel = async_decode_kernel_for(bits, head_dim, group_size, kv_heads, true);
+  p.streaming = true;
+  p.path = KVSSD_B200_PATH_TENSOR_CORE;
+  p.heads_per_cta = kv_heads;
+  p.wph = async_warps() / kv_heads;
+  p.threads = async_threads();
+  p.n_head_groups = 1;
+  p.tiles_per_block = (block_tokens + 15) / 16;
+  bp.ctas = std::max(1, info.sms / n_problems);
+  p.n_splits = bp.ctas;
+  p.n_parts = bp.ctas * n_problems;
+  if (kProblemTicketOffset + static_cast<size_t>(2) * n_problems * sizeof(unsigned) > kHeaderBytes)
+    return fail(KVSSD_B200_ERR_UNSUPPORTED, "too many problems for the workspace header");
+  bp.ws_bytes = kHeaderBytes +
+                static_cast<size_t>(p.n_parts) * query_heads * (head_dim + 2) * sizeof(float);
+  return KVSSD_B200_OK;
+}
+
+}  // namespace
+}  // namespace kvb
+
+extern "C" {
+
+int kvssd_b200_decode_batched_workspace_size(int n_problems, int block_tokens, int query_heads,
+                                             int kv_heads, int head_dim, int bits,
+                                             int group_size, size_t* bytes) {
+  if (!bytes) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "bytes must not be NULL");
+  BatchPlan bp;
+  const int st = plan_batched(n_problems, block_tokens, query_heads, kv_heads, head_dim, bits,
+                              group_size, bp);
+  if (st) return st;
+  *bytes = bp.ws_bytes;
+  return KVSSD_B200_OK;
+}
+
+int kvssd_b200_decode_batched(const kvssd_b200_problem* problems, int n_problems,
+                              int query_dtype, int block_tokens, int query_heads, int kv_heads,
+                              int head_dim, int bits, int group_size, float sm_scale,
+                              void* workspace, size_t workspace_bytes,
+                              kvssd_b200_stream_t stream) {
+  if (!problems) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "problems must not be NULL");
+  if (query_dtype < KVSSD_B200_Q_F32 || query_dtype > KVSSD_B200_Q_F64)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "unknown query dtype");
+  if (!std::isfinite(sm_scale)) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "sm_scale must be finite");
+  BatchPlan bp;
+  int st = plan_batched(n_problems, block_tokens, query_heads, kv_heads, head_dim, bits,
+                        group_size, bp);
+  if (st) return st;
+  if (!workspace || workspace_bytes < bp.ws_bytes)
+    return fail(KVSSD_B200_ERR_WORKSPACE, "workspace needs " + std::to_string(bp.ws_bytes) + " bytes");
+  if (reinterpret_cast<uintptr_t>(workspace) & 15u)
+    return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+  const Plan& p = bp.p;
+  DecodeArgs a{};
+  a.q_dtype = query_dtype;
+  a.bt = block_tokens;
+  a.qh = query_heads;
+  a.kvh = kv_heads;
+  a.d = head_dim;
+  a.bits = bits;
+  a.group = group_size;
+  a.gqa = p.gqa;
+  a.n_qsub = p.n_qsub;
+  a.n_vheads = p.n_vheads;
+  a.heads_per_cta = p.heads_per_cta;
+  a.wph = p.wph;
+  a.tiles_per_block = p.tiles_per_block;
+  a.n_splits = bp.ctas;
+  a.score_scale = sm_scale * 1.4426950408889634f;
+  char* ws = static_cast<char*>(workspace);
+  a.status = reinterpret_cast<unsigned*>(ws);
+  a.problem_tickets = reinterpret_cast<unsigned*>(ws + kProblemTicketOffset);
+  a.part_ml = reinterpret_cast<float*>(ws + kHeaderBytes);
+  a.part_acc = a.part_ml + static_cast<size_t>(p.n_parts) * query_heads * 2;
+  a.problems = problems;
+  a.fuse_combine = 1;
+  {
+    cudaError_t e = ensure_dynamic_smem(p.kernel, p.smem);
+    if (e != cudaSuccess) return cuda_fail(e, "shared-memory attribute");
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(bp.ctas, n_problems, 1);
+  cfg.blockDim = dim3(p.threads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, p.kernel, a);
+  if (e == cudaErrorCooperativeLaunchTooLarge) {
+    cudaGetLastError();
+    return fail(KVSSD_B200_ERR_UNSUPPORTED, "the batched grid cannot be co-resident here");
+  }
+  return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "batched decode launch");
 }
 
 int kvssd_b200_read_status(void* workspace, int clear, unsigned* device_status,

@@ -103,4 +103,42 @@ __device__ __forceinline__ void combine_slice(const float* __restrict__ part_acc
   }
 }
 
+// One warp folds all n_parts (<= 32) parts of a slice: lane j loads part j's m and l, every
+// lane its dim of each part's row (all loads issued before use), then the weights reach the
+// lanes by shuffle. Writes the slice's normalised output and natural-log LSE.
+__device__ __forceinline__ void combine_slice_warp(const float* __restrict__ part_acc,
+                                                   const float* __restrict__ part_ml,
+                                                   int n_parts, int qh, int d, int h, int chunk,
+                                                   float* __restrict__ out,
+                                                   float* __restrict__ lse) {
+  const int lane = threadIdx.x & 31;
+  const int dd = chunk * 32 + lane;
+  const bool has_dim = dd < d;
+  float mp = -INFINITY, lp = 0.f;
+  if (lane < n_parts) {
+    const float2 ml =
+        __ldcg(reinterpret_cast<const float2*>(part_ml + (static_cast<size_t>(lane) * qh + h) * 2));
+    mp = ml.x;
+    lp = ml.y;
+  }
+  const float* row = part_acc + static_cast<size_t>(h) * d + dd;
+  const size_t stride = static_cast<size_t>(qh) * d;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = (j < n_parts && has_dim) ? __ldcg(row + j * stride) : 0.f;
+  float mx = mp;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float wp = (mp == -INFINITY || mx == -INFINITY) ? 0.f : exp2f(mp - mx);
+  float ls = wp * lp;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+  float t = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) t = fmaf(__shfl_sync(0xffffffffu, wp, j), v[j], t);
+  const bool empty = (mx == -INFINITY) || !(ls > 0.f);
+  if (has_dim) out[static_cast<size_t>(h) * d + dd] = empty ? 0.f : t / ls;
+  if (chunk == 0 && lane == 0) lse[h] = empty ? -INFINITY : (mx + log2f(ls)) * kLn2;
+}
+
 }  // namespace kvb

@@ -31,6 +31,7 @@ enum DeviceStatusBits : unsigned {
   kDevBadValidCount = 2u,   // a valid_tokens entry outside [0, block_tokens]
   kDevCombineTimeout = 4u,  // a fused combine gave up waiting for the other CTAs' parts
   kDevExchangeTimeout = 8u,  // a cross-GPU exchange gave up waiting for another rank's slice
+  kDevBadProblem = 16u,      // a batched problem descriptor was refused (misaligned/invalid)
 };
 
 // The G FP16 scales of one (token, KV head) row, loaded as one 8- or 4-byte word.

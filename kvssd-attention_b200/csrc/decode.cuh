@@ -15,6 +15,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "../../include/kvssd_b200.h"
+
 namespace kvb {
 
 constexpr int kMaxExchangeRanks = 8;
@@ -51,6 +53,10 @@ struct DecodeArgs {
   int xworld;
   int xrank;
   uint8_t* xpeers[kMaxExchangeRanks];  // every rank's exchange buffer ([xrank] is local)
+  // Batched decode: problem blockIdx.y of this device array (nullptr: one problem, the
+  // fields above); each problem's tickets are 2 words at problem_tickets + 2 * problem.
+  const kvssd_b200_problem* problems;
+  unsigned* problem_tickets;
 };
 
 // Exchange buffer layout for `world` ranks and n_slices = qh * ceil(d / 32) slices:

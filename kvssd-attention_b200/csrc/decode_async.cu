@@ -105,7 +105,7 @@ struct WarpFeed {
 };
 
 template <int KVH, int GROUP>
-__global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const DecodeArgs a) {
+__device__ __forceinline__ void async_decode_body(const DecodeArgs& a) {
   constexpr int D = 128, BITS = 4, G = D / GROUP, MT = D / 16, DEPTH = kAsyncDepth;
   constexpr int PD = D * BITS / 8;            // 64 bytes of codes per (token, head)
   constexpr int SB = 2 * G;                   // scale bytes per (token, head)
@@ -386,27 +386,74 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const De
   if (a.fuse_combine) fused_combine_tail<D>(a, epoch, a.n_splits);
 }
 
+template <int KVH, int GROUP>
+__global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_kernel(const DecodeArgs a) {
+  async_decode_body<KVH, GROUP>(a);
+}
+
+// Batched decode: problem blockIdx.y of a.problems, its splits along x. The problem's fields
+// replace the single-problem ones; its parts and tickets are its own slices of the workspace.
+template <int KVH, int GROUP>
+__global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_batched_kernel(const DecodeArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the descriptors may be fresh
+  const kvssd_b200_problem pd = a.problems[blockIdx.y];
+  // The host cannot see device-resident descriptors: refuse operands the copies and loads
+  // cannot take (every CTA of the problem reaches the same verdict, so none waits for it).
+  const int qsize = a.q_dtype == kQF64 ? 8 : a.q_dtype == kQF32 ? 4 : 2;
+  const uintptr_t a16 = reinterpret_cast<uintptr_t>(pd.packed_k) | reinterpret_cast<uintptr_t>(pd.packed_v) |
+                        reinterpret_cast<uintptr_t>(pd.scales_k) | reinterpret_cast<uintptr_t>(pd.scales_v);
+  const uintptr_t a4 = reinterpret_cast<uintptr_t>(pd.valid_tokens) |
+                       reinterpret_cast<uintptr_t>(pd.block_table) |
+                       reinterpret_cast<uintptr_t>(pd.out) | reinterpret_cast<uintptr_t>(pd.lse);
+  if (!pd.packed_k || !pd.packed_v || !pd.scales_k || !pd.scales_v || !pd.valid_tokens ||
+      !pd.query || !pd.out || !pd.lse || (a16 & 15u) || (a4 & 3u) ||
+      (reinterpret_cast<uintptr_t>(pd.query) % qsize) || pd.n_pool_blocks < 1 ||
+      pd.n_sel_blocks < 0) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.status, kDevBadProblem);
+    return;
+  }
+  DecodeArgs b = a;
+  b.q = pd.query;
+  b.kp = pd.packed_k;
+  b.vp = pd.packed_v;
+  b.ks = reinterpret_cast<const __half*>(pd.scales_k);
+  b.vs = reinterpret_cast<const __half*>(pd.scales_v);
+  b.valid = pd.valid_tokens;
+  b.table = pd.block_table;
+  b.n_pool = pd.n_pool_blocks;
+  b.n_sel = pd.n_sel_blocks;
+  b.total_tiles = static_cast<long long>(pd.n_sel_blocks) * a.tiles_per_block;
+  b.out = pd.out;
+  b.lse = pd.lse;
+  const size_t parts = static_cast<size_t>(blockIdx.y) * a.n_splits * a.qh;
+  b.part_ml = a.part_ml + parts * 2;
+  b.part_acc = a.part_acc + parts * a.d;
+  b.tickets = a.problem_tickets + 2 * blockIdx.y;
+  async_decode_body<KVH, GROUP>(b);
+}
+
 using DecodeKernel = void (*)(const DecodeArgs);
 
 // INT4, head_dim 128, group_size 32 or 64 (16-byte code chunks inside one scale group; scale
 // rows of whole 4-byte words), KV heads dividing the 16 warps of a CTA.
 template <int GROUP>
-DecodeKernel async_kernel_for_heads(int kvh) {
+DecodeKernel async_kernel_for_heads(int kvh, bool batched) {
   switch (kvh) {
-    case 1: return async_decode_kernel<1, GROUP>;
-    case 2: return async_decode_kernel<2, GROUP>;
-    case 4: return async_decode_kernel<4, GROUP>;
-    case 8: return async_decode_kernel<8, GROUP>;
-    case 16: return async_decode_kernel<16, GROUP>;
+    case 1: return batched ? async_decode_batched_kernel<1, GROUP> : async_decode_kernel<1, GROUP>;
+    case 2: return batched ? async_decode_batched_kernel<2, GROUP> : async_decode_kernel<2, GROUP>;
+    case 4: return batched ? async_decode_batched_kernel<4, GROUP> : async_decode_kernel<4, GROUP>;
+    case 8: return batched ? async_decode_batched_kernel<8, GROUP> : async_decode_kernel<8, GROUP>;
+    case 16:
+      return batched ? async_decode_batched_kernel<16, GROUP> : async_decode_kernel<16, GROUP>;
     default: return nullptr;
   }
 }
 
-DecodeKernel async_decode_kernel_for(int bits, int d, int group, int kvh) {
+DecodeKernel async_decode_kernel_for(int bits, int d, int group, int kvh, bool batched) {
   if (bits != 4 || d != 128) return nullptr;
   switch (group) {
-    case 32: return async_kernel_for_heads<32>(kvh);
-    case 64: return async_kernel_for_heads<64>(kvh);
+    case 32: return async_kernel_for_heads<32>(kvh, batched);
+    case 64: return async_kernel_for_heads<64>(kvh, batched);
     default: return nullptr;
   }
 }

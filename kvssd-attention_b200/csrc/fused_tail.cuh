@@ -121,6 +121,18 @@ __device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned
   }
   if (k < 0) return;
   __syncthreads();
+  if (a.xworld == 0 && n_parts <= 32) {
+    // Few parts (a batched problem's handful of CTAs): one warp folds a whole slice, so the
+    // CTA's 16 warps work on 16 of its slices at once.
+    const int warp = threadIdx.x >> 5, n_warps = blockDim.x >> 5;
+    const int mine = (n_slices - k + n_comb - 1) / n_comb;  // slices k, k + n_comb, ...
+    for (int j = warp; j < mine; j += n_warps) {
+      const int sl = k + j * n_comb;
+      combine_slice_warp(a.part_acc, a.part_ml, n_parts, a.qh, D, sl / kChunks, sl % kChunks,
+                         a.out, a.lse);
+    }
+    __syncthreads();
+  } else {
   for (int sl = k; sl < n_slices; sl += n_comb) {
     if (a.xworld == 0) {
       combine_slice(a.part_acc, a.part_ml, n_parts, a.qh, D, sl / kChunks, sl % kChunks,
@@ -131,6 +143,7 @@ __device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned
                            sl % kChunks, &o, &l2);
       if (threadIdx.x < 32) exchange_slice<D>(a, epoch, sl, n_slices, o, l2);
     }
+  }
   }
   if (threadIdx.x == 0) {
     if (atomicAdd(a.tickets + 1, 1u) == static_cast<unsigned>(n_comb) - 1) {

@@ -22,6 +22,7 @@ ERR_DEVICE_STATUS = 5
 Q_F32, Q_F16, Q_BF16, Q_F64 = 0, 1, 2, 3
 IPC_HANDLE_BYTES = 64
 DEV_BAD_BLOCK, DEV_BAD_VALID, DEV_COMBINE_TIMEOUT, DEV_EXCHANGE_TIMEOUT = 1, 2, 4, 8
+DEV_BAD_PROBLEM = 16
 PATH_AUTO, PATH_TENSOR_CORE, PATH_GENERIC, PATH_TENSOR_CORE_REGS = 0, 1, 2, 3
 
 _c_int = ctypes.c_int
@@ -75,6 +76,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "kvssd_b200_set_path_override": (_c_int, [_c_int]),
     "kvssd_b200_read_status": (_c_int, [_c_void, _c_int, _c_uint_p, _c_void]),
+    "kvssd_b200_decode_batched_workspace_size": (
+        _c_int, [_c_int] * 7 + [ctypes.POINTER(_c_size)]
+    ),
+    "kvssd_b200_decode_batched": (
+        _c_int,
+        [_c_void, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float,
+         _c_void, _c_size, _c_void],
+    ),
     "kvssd_b200_decode_records": (
         _c_int,
         [_c_void, _c_size, _c_int, _c_int, _c_void, _c_int, _c_int, _c_int, _c_int, _c_int,

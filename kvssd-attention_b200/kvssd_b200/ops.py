@@ -22,7 +22,7 @@ _QUERY_DTYPES = {
     torch.float64: _native.Q_F64,
 }
 
-_WORKSPACE_HEADER = 256
+_WORKSPACE_HEADER = 2048
 
 
 class _Workspaces:
@@ -196,6 +196,81 @@ def decode_exchange(query, packed_k, packed_v, scales_k, scales_v, valid_tokens,
         )
         _native.check(status, "kvssd_b200_decode_exchange")
     return out, lse
+
+
+class BatchedDecode:
+    """Several independent decodes in ONE launch (kvssd_b200_decode_batched).
+
+    ``problems``: sequence of (query, packed_k, packed_v, scales_k, scales_v, valid_tokens,
+    block_table or None) sharing the geometry (INT4, head_dim 128, group 32/64). The device
+    descriptor table, the outputs and the workspace are built once, so ``run()`` is a single
+    launch with no host-to-device copy: it can be captured in a CUDA graph and replayed (the
+    tensors the descriptors point to may be refilled in place between replays).
+    """
+
+    def __init__(self, problems, bits: int, group_size: int, sm_scale: float):
+        problems = list(problems)
+        if not problems:
+            raise ValueError("at least one problem is required")
+        self.bits, self.group_size, self.sm_scale = bits, group_size, float(sm_scale)
+        checked = []
+        geom0 = None
+        for prob in problems:
+            query, kp, vp, ks, vs, valid, table = prob
+            query, geom = _decode_args(query, kp, vp, ks, vs, valid, bits, group_size, table)
+            n_pool, n_sel, bt, qh, kvh, d, _, _ = geom
+            if geom0 is None:
+                geom0 = (bt, qh, kvh, d, query.dtype, query.device)
+            elif (bt, qh, kvh, d, query.dtype, query.device) != geom0:
+                raise ValueError("batched problems must share geometry, query dtype and device")
+            checked.append((query, kp, vp, ks, vs, valid, table, n_pool, n_sel))
+        self.geometry = geom0
+        bt, qh, kvh, d, qdtype, device = geom0
+        self.device = device
+        self._keep = checked  # the tensors the descriptors point to
+        self.outs = [(torch.empty((qh, d), dtype=torch.float32, device=device),
+                      torch.empty((qh,), dtype=torch.float32, device=device)) for _ in checked]
+        desc = torch.empty((len(checked), 10), dtype=torch.int64, pin_memory=True)
+        for i, ((query, kp, vp, ks, vs, valid, table, n_pool, n_sel), (out, lse)) in enumerate(
+                zip(checked, self.outs)):
+            desc[i] = torch.tensor([_ptr(query), _ptr(kp), _ptr(vp), _ptr(ks), _ptr(vs),
+                                    _ptr(valid), _ptr(table) or 0, _ptr(out), _ptr(lse),
+                                    (n_pool & 0xFFFFFFFF) | (n_sel << 32)], dtype=torch.int64)
+        self.descriptors = desc.to(device)
+        need = ctypes.c_size_t()
+        with torch.cuda.device(device):
+            _native.check(_native.library().kvssd_b200_decode_batched_workspace_size(
+                len(checked), bt, qh, kvh, d, bits, group_size, ctypes.byref(need)),
+                "kvssd_b200_decode_batched_workspace_size")
+        self.workspace = torch.zeros(need.value, dtype=torch.uint8, device=device)
+        torch.cuda.synchronize(device)
+
+    def run(self) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        bt, qh, kvh, d, qdtype, device = self.geometry
+        with torch.cuda.device(device):
+            _native.check(_native.library().kvssd_b200_decode_batched(
+                _ptr(self.descriptors), len(self.outs), _QUERY_DTYPES[qdtype], bt, qh, kvh, d,
+                self.bits, self.group_size, self.sm_scale, _ptr(self.workspace),
+                self.workspace.numel(), _stream_handle(device)),
+                "kvssd_b200_decode_batched")
+        return self.outs
+
+    def read_status(self, clear: bool = True) -> int:
+        """The sticky device status word of this batch's workspace (bit 16: a refused
+        descriptor; see read_device_status for the others)."""
+        value = ctypes.c_uint()
+        with torch.cuda.device(self.device):
+            status = _native.library().kvssd_b200_read_status(
+                _ptr(self.workspace), 1 if clear else 0, ctypes.byref(value),
+                _stream_handle(self.device))
+        if status not in (_native.OK, _native.ERR_DEVICE_STATUS):
+            _native.check(status, "kvssd_b200_read_status")
+        return int(value.value)
+
+
+def decode_batched(problems, bits: int, group_size: int, sm_scale: float):
+    """One-shot BatchedDecode: builds the descriptors and launches; returns [(out, lse), ...]."""
+    return BatchedDecode(problems, bits, group_size, sm_scale).run()
 
 
 RECORD_BAD_HEADER, RECORD_BAD_GEOMETRY, RECORD_BAD_LENGTH, RECORD_BAD_CRC = 1, 2, 4, 8
