@@ -55,8 +55,10 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pipeline", action="store_true",
                     help="skip the KVSSDPipeline and record-decode legs")
-    ap.add_argument("--path", choices=["auto", "stream", "regs", "generic"], default="auto",
-                    help="A/B: force the cp.async-streamed, register-fed or CUDA-core decode kernel")
+    ap.add_argument("--path", choices=["auto", "stream", "cpasync", "regs", "generic"],
+                    default="auto",
+                    help="A/B: force the tensor-core family (TMA-fed streaming where it "
+                         "qualifies), the cp.async-fed streaming, register-fed or CUDA-core kernel")
     ap.add_argument("--eager", action="store_true",
                     help="launch the timed device-resident steps one by one instead of "
                          "replaying them from a CUDA graph")
@@ -263,6 +265,33 @@ def pipeline_legs(w, base, q, scale, device, rank, args) -> dict:
     }
 
 
+def graph_time(fn, device, reps: int = 20) -> float:
+    """Device ms per call of ``fn``: ``reps`` calls captured in one CUDA graph (after 3 eager
+    warm-up calls and one on the capture stream), one warm replay, then one timed replay."""
+    stream = torch.cuda.current_stream(device)
+    for _ in range(3):
+        fn()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        fn()
+    stream.wait_stream(side)
+    torch.cuda.synchronize(device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    del g
+    return e0.elapsed_time(e1) / reps
+
+
 def c4_legs(w, base, device, args) -> dict:
     """The multi-layer step of c4 on one GPU: 32 layers x 65536 tokens (each layer 512 blocks of
     distinct memory: halves of 16 copies of this workload's pool), each with its own query,
@@ -279,35 +308,10 @@ def c4_legs(w, base, device, args) -> dict:
                for _ in range(layers)]
     problems = [(q, *p, None) for q, p in zip(queries, pools)]
     scale = 1 / math.sqrt(w.head_dim)
-    stream = torch.cuda.current_stream(device)
-
-    def graph_time(fn, reps: int = 20) -> float:
-        for _ in range(3):
-            fn()
-        side = torch.cuda.Stream(device)
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            fn()
-        stream.wait_stream(side)
-        torch.cuda.synchronize(device)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=side):
-            for _ in range(reps):
-                fn()
-        g.replay()
-        torch.cuda.synchronize(device)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        g.replay()
-        e1.record(stream)
-        torch.cuda.synchronize(device)
-        del g
-        return e0.elapsed_time(e1) / reps
-
     batch = ops.BatchedDecode(problems, w.bits, w.group_size, scale)
-    batched_ms = graph_time(batch.run)
+    batched_ms = graph_time(batch.run, device)
     single_ms = graph_time(lambda: [ops.decode(q, *p, w.bits, w.group_size, scale)
-                                    for q, p in zip(queries, pools)])
+                                    for q, p in zip(queries, pools)], device)
     step_bytes = layers * per * w.bytes_per_block
     return {
         "workload": "c4 on 1 GPU: 32 layers x 65536 tokens, INT4 g32, 8 KV heads, GQA 4",
@@ -317,6 +321,37 @@ def c4_legs(w, base, device, args) -> dict:
                                  "GB/s": step_bytes / (single_ms * 1e-3) / 1e9},
         "bytes_per_step": step_bytes,
     }
+
+
+def small_config_legs(device) -> dict:
+    """Latency of the other single-GPU configurations (device time per decode, CUDA-graph
+    replays): c1 (8192 tokens, INT4, all 64 blocks) and c3 (INT2 with 1 % outlier channels x8,
+    RecentSinkBlocks(1, 32) over 1024 blocks: 33 blocks through a block table)."""
+    from kvssd_b200 import RecentSinkBlocks, ops
+    from kvssd_b200.workloads import WORKLOADS, make_layer
+
+    res = {}
+    for name in ("c1", "c3"):
+        w = WORKLOADS[name]
+        lay = make_layer(w, 0, "cpu")
+        t = [x.to(device) for x in (lay.query, lay.packed_k, lay.packed_v, lay.scales_k,
+                                    lay.scales_v, lay.valid_tokens)]
+        sel = list(range(lay.packed_k.shape[0]))
+        table = None
+        if w.sink is not None:
+            sel = RecentSinkBlocks(w.sink, w.recent).select(sel)
+            table = torch.tensor(sel, dtype=torch.int32, device=device)
+        scale = 1 / math.sqrt(w.head_dim)
+        us = graph_time(lambda: ops.decode(*t, w.bits, w.group_size, scale, block_table=table),
+                        device, reps=50) * 1e3
+        nbytes = len(sel) * w.bytes_per_block
+        plan = ops.decode_plan(len(sel), w.block_tokens, w.query_heads, w.kv_heads, w.head_dim,
+                               w.bits, w.group_size)
+        res[name] = {"us_per_decode": us, "GB/s": nbytes / (us * 1e-6) / 1e9,
+                     "inputs": "resident, L2-warm between replays (a latency figure)",
+                     "selected_blocks": len(sel), "packed_kv_bytes": nbytes,
+                     "kernel": plan["kernel"]}
+    return res
 
 
 def run_ours(args) -> None:
@@ -334,6 +369,7 @@ def run_ours(args) -> None:
     torch.cuda.set_device(device)
     from kvssd_b200 import _native
     ops.set_path_override({"auto": _native.PATH_AUTO, "stream": _native.PATH_TENSOR_CORE,
+                           "cpasync": _native.PATH_TENSOR_CORE_CPASYNC,
                            "regs": _native.PATH_TENSOR_CORE_REGS,
                            "generic": _native.PATH_GENERIC}[args.path])
     dist = None
@@ -449,7 +485,7 @@ def run_ours(args) -> None:
     # whole decode; the other kernels are timed without their separate combine launch.
     plan = ops.decode_plan(w.blocks_per_layer, w.block_tokens, w.query_heads, w.kv_heads,
                            w.head_dim, w.bits, w.group_size)
-    fused = plan["kernel"] == "tensor_core_stream"
+    fused = plan["kernel"] in ops.STREAMING_KERNELS
 
     def local_decode(i: int):
         p = pools[i % len(pools)]
@@ -469,14 +505,18 @@ def run_ours(args) -> None:
         kernel_ms = timed(local_decode, args.steps, 3, graph=not args.eager)
     else:
         kernel_ms = split_ms
-    kernel_name = {"tensor_core_stream": "async_decode_kernel", "tensor_core_regs": "tc_decode_kernel",
+    kernel_name = {"tensor_core_tma": "tma_decode_kernel",
+                   "tensor_core_stream": "async_decode_kernel",
+                   "tensor_core_regs": "tc_decode_kernel",
                    "generic": "simt_decode_kernel"}[plan["kernel"]]
     peak, peak_kind = peaks()
     achieved = nbytes / (kernel_ms * 1e-3) / 1e9
     traffic = None
     tfile = ROOT / "profiles" / "decode_c2_traffic.json"
-    if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch")
+    if tfile.exists():  # the ncu capture of the same kernel (null if it was another kernel)
+        tinfo = json.loads(tfile.read_text())
+        if kernel_name in tinfo.get("kernel", ""):
+            traffic = tinfo.get("dram_bytes_per_launch")
 
     # ---- end to end through the plugin with host buffers (H2D + decode + D2H each step)
     backend = B200AttentionBackend()
@@ -507,9 +547,11 @@ def run_ours(args) -> None:
     # alone on the layer's records resident in HBM.
     pipeline = None
     c4 = None
+    small = None
     if not args.no_pipeline and world == 1:
         pipeline = pipeline_legs(w, base, q, scale, device, rank, args)
         c4 = c4_legs(w, base, device, args)
+        small = small_config_legs(device)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -571,6 +613,8 @@ def run_ours(args) -> None:
         record["pipeline"] = pipeline
     if c4 is not None:
         record["c4_multi_layer"] = c4
+    if small is not None:
+        record["c1_c3_latency"] = small
     emit(record)
 
 

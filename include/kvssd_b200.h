@@ -56,10 +56,14 @@ enum kvssd_b200_query_dtype {
 enum kvssd_b200_path {
   KVSSD_B200_PATH_AUTO = 0,
   KVSSD_B200_PATH_TENSOR_CORE = 1,     /* mma.sync split-KV tile math (head_dim 64/128/256,
-                                          group >= 16); cp.async-streamed where it qualifies */
+                                          group >= 16); streamed where it qualifies: TMA-fed
+                                          (INT4, head_dim 128, 4/8/16 KV heads), else
+                                          cp.async-fed */
   KVSSD_B200_PATH_GENERIC = 2,         /* CUDA-core split-KV kernel (any head_dim <= 256) */
-  KVSSD_B200_PATH_TENSOR_CORE_REGS = 3 /* override only: tensor-core tile math fed by
+  KVSSD_B200_PATH_TENSOR_CORE_REGS = 3, /* override only: tensor-core tile math fed by
                                           per-thread global loads (no shared-memory ring) */
+  KVSSD_B200_PATH_TENSOR_CORE_CPASYNC = 4 /* the streaming kernel fed by per-warp cp.async
+                                          rings (as an override: never the TMA-fed one) */
 };
 
 /* Library ABI version (incremented on any signature change). No reference counterpart. */
@@ -143,7 +147,8 @@ KVSSD_B200_API int kvssd_b200_decode_combine(const void* workspace, int n_parts,
 KVSSD_B200_API int kvssd_b200_decode_path(int head_dim, int bits, int group_size, int* path);
 
 /* Launch plan kvssd_b200_decode would use on the current device for 16-byte aligned operands:
- * *kernel = KVSSD_B200_PATH_TENSOR_CORE (streamed), _TENSOR_CORE_REGS or _GENERIC; the number of
+ * *kernel = KVSSD_B200_PATH_TENSOR_CORE (TMA-fed streaming kernel), _TENSOR_CORE_CPASYNC
+ * (cp.async-fed streaming kernel), _TENSOR_CORE_REGS or _GENERIC; the number of
  * split CTAs and of (m, l, acc) parts. No reference counterpart. */
 KVSSD_B200_API int kvssd_b200_decode_plan(int n_sel_blocks, int block_tokens, int query_heads,
                                           int kv_heads, int head_dim, int bits, int group_size,
@@ -272,7 +277,8 @@ KVSSD_B200_API int kvssd_b200_decode_exchange(const void* query, int query_dtype
  * workspace; *device_status receives the OR of flagged conditions (1 = block-table entry out
  * of range, 2 = valid_tokens entry out of [0, block_tokens], 4 = a fused combine gave up after
  * waiting about a second for the other CTAs' parts, 8 = a cross-GPU exchange gave up waiting
- * for another rank; out/lse of a timed-out call are invalid). Returns
+ * for another rank, 16 = a batched problem descriptor was refused, 32 = a TMA-fed kernel gave
+ * up waiting for its copies; out/lse of a timed-out call are invalid). Returns
  * KVSSD_B200_ERR_DEVICE_STATUS when it is nonzero. No reference counterpart. */
 KVSSD_B200_API int kvssd_b200_read_status(void* workspace, int clear, unsigned* device_status,
                            kvssd_b200_stream_t stream);

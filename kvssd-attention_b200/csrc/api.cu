@@ -28,6 +28,10 @@ int async_threads();
 int async_warps();
 int async_depth();
 int async_stage_bytes(int group);
+bool tma_decode_supported(int bits, int d, int group, int kvh, int bt);
+size_t tma_decode_smem(int kvh, int group);
+int tma_decode_threads(int kvh, int group);
+cudaError_t launch_tma_decode(const DecodeArgs& a, int n_splits, cudaStream_t s);
 using DequantKernel = void (*)(const uint8_t*, const __half*, long long, int, int, __half*,
                                uint8_t*);
 DequantKernel dequant_kernel_for(int bits, int mode);
@@ -116,7 +120,8 @@ int check_geometry(const Geometry& g) {
 
 struct Plan {
   int path = 0;
-  bool streaming = false;  // cp.async-fed kernel with per-warp shared-memory rings
+  bool streaming = false;  // streaming kernel (fused combine): TMA-fed or cp.async-fed
+  bool tma = false;        // streaming kernel fed by TMA copies into a CTA ring
   size_t smem = 0;
   DecodeKernel kernel = nullptr;
   int gqa = 0, n_qsub = 0, n_vheads = 0, heads_per_cta = 0, wph = 0, n_head_groups = 0;
@@ -129,26 +134,44 @@ int choose_path(int d, int bits, int group) {
   const bool tc_ok = tc_decode_kernel_for(bits, d, group) != nullptr;
   if (g_path_override == KVSSD_B200_PATH_GENERIC) return KVSSD_B200_PATH_GENERIC;
   if (g_path_override == KVSSD_B200_PATH_TENSOR_CORE ||
-      g_path_override == KVSSD_B200_PATH_TENSOR_CORE_REGS)
+      g_path_override == KVSSD_B200_PATH_TENSOR_CORE_REGS ||
+      g_path_override == KVSSD_B200_PATH_TENSOR_CORE_CPASYNC)
     return tc_ok ? KVSSD_B200_PATH_TENSOR_CORE : -1;
   return tc_ok ? KVSSD_B200_PATH_TENSOR_CORE : KVSSD_B200_PATH_GENERIC;
 }
 
 
-// Shared memory of the streaming kernel (a private cp.async ring per warp); false if the
-// geometry does not qualify (INT4, head_dim 128, group 32 or 64, KV heads dividing the 16
-// warps, at most 8 query heads per KV head).
-bool plan_streaming(const Geometry& g, const DeviceInfo& info, Plan& p) {
+// Streaming kernel choice and shared memory; false if the geometry does not qualify (INT4,
+// head_dim 128, group 32 or 64, KV heads dividing the 16 warps, at most 8 query heads per KV
+// head). The TMA-fed kernel is preferred (KV heads 4, 8 or 16, block_tokens a multiple of 16,
+// token rows of the pool addressable by 32-bit TMA coordinates: pool_rows < 2^31, 0 when
+// unknown); otherwise the per-warp cp.async rings.
+bool plan_streaming(const Geometry& g, const DeviceInfo& info, Plan& p, bool allow_tma,
+                    long long pool_rows) {
+  p.tma = false;
+  if (g.bits != 4 || g.d != 128 || p.n_qsub != 1 || async_warps() % g.kvh) return false;
+  const size_t merge_bytes = static_cast<size_t>(async_warps() - g.kvh) * 32 * (4 + 4 * (g.d / 16)) * 4;
+  const size_t max_smem = static_cast<size_t>(info.max_smem_optin) - 1024;
+  if (allow_tma && g_path_override != KVSSD_B200_PATH_TENSOR_CORE_CPASYNC &&
+      pool_rows < (1LL << 31) && tma_decode_supported(g.bits, g.d, g.group, g.kvh, g.bt)) {
+    const size_t smem = tma_decode_smem(g.kvh, g.group);
+    if (smem <= max_smem && merge_bytes + 1024 <= smem) {
+      p.tma = true;
+      p.kernel = nullptr;
+      p.smem = smem;
+      return true;
+    }
+  }
   p.kernel = async_decode_kernel_for(g.bits, g.d, g.group, g.kvh, false);
   if (p.kernel == nullptr) return false;
-  if (p.n_qsub != 1 || async_warps() % g.kvh) return false;
   p.smem = static_cast<size_t>(async_warps()) * async_depth() * async_stage_bytes(g.group);
-  const size_t merge_bytes = static_cast<size_t>(async_warps() - g.kvh) * 32 * (4 + 4 * (g.d / 16)) * 4;
-  return p.smem <= static_cast<size_t>(info.max_smem_optin) - 1024 && merge_bytes <= p.smem;
+  return p.smem <= max_smem && merge_bytes <= p.smem;
 }
 
-// aligned: packed K/V 16-byte aligned; allow_stream: scales 16-byte aligned as well.
-int make_plan(const Geometry& g, bool aligned, bool allow_stream, Plan& p) {
+// aligned: packed K/V 16-byte aligned; allow_stream: scales 16-byte aligned as well;
+// pool_rows: n_pool_blocks * block_tokens (0 when unknown).
+int make_plan(const Geometry& g, bool aligned, bool allow_stream, Plan& p,
+              long long pool_rows = 0) {
   int st = check_geometry(g);
   if (st) return st;
   int dev = 0;
@@ -167,7 +190,8 @@ int make_plan(const Geometry& g, bool aligned, bool allow_stream, Plan& p) {
   p.n_qsub = (p.gqa + 7) / 8;
   p.n_vheads = g.kvh * p.n_qsub;
   if (p.path == KVSSD_B200_PATH_TENSOR_CORE && aligned && allow_stream &&
-      g_path_override != KVSSD_B200_PATH_TENSOR_CORE_REGS && plan_streaming(g, info, p)) {
+      g_path_override != KVSSD_B200_PATH_TENSOR_CORE_REGS &&
+      plan_streaming(g, info, p, true, pool_rows)) {
     p.streaming = true;
     p.heads_per_cta = g.kvh;
     p.wph = async_warps() / g.kvh;
@@ -180,7 +204,8 @@ int make_plan(const Geometry& g, bool aligned, bool allow_stream, Plan& p) {
     p.heads_per_cta = 1;
     p.wph = 4;
   }
-  p.threads = p.streaming ? async_threads() : 32 * p.heads_per_cta * p.wph;
+  p.threads = p.streaming ? (p.tma ? tma_decode_threads(g.kvh, g.group) : async_threads())
+                          : 32 * p.heads_per_cta * p.wph;
   p.n_head_groups = (p.n_vheads + p.heads_per_cta - 1) / p.heads_per_cta;
   p.tiles_per_block = (g.bt + 15) / 16;
   p.total_tiles = static_cast<long long>(g.n_sel) * p.tiles_per_block;
@@ -275,7 +300,8 @@ int kvssd_b200_decode_plan(int n_sel_blocks, int block_tokens, int query_heads, 
   const int st = make_plan(g, true, true, p);
   if (st) return st;
   *kernel = p.path == KVSSD_B200_PATH_GENERIC ? KVSSD_B200_PATH_GENERIC
-            : p.streaming                        ? KVSSD_B200_PATH_TENSOR_CORE
+            : p.tma                              ? KVSSD_B200_PATH_TENSOR_CORE
+            : p.streaming                        ? KVSSD_B200_PATH_TENSOR_CORE_CPASYNC
                                                  : KVSSD_B200_PATH_TENSOR_CORE_REGS;
   *n_splits = p.n_splits;
   *n_parts = p.n_parts;
@@ -283,7 +309,7 @@ int kvssd_b200_decode_plan(int n_sel_blocks, int block_tokens, int query_heads, 
 }
 
 int kvssd_b200_set_path_override(int path) {
-  if (path < KVSSD_B200_PATH_AUTO || path > KVSSD_B200_PATH_TENSOR_CORE_REGS)
+  if (path < KVSSD_B200_PATH_AUTO || path > KVSSD_B200_PATH_TENSOR_CORE_CPASYNC)
     return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "unknown path");
   g_path_override = path;
   return KVSSD_B200_OK;
@@ -313,7 +339,8 @@ int prepare_decode(const void* query, int query_dtype, const uint8_t* packed_k,
     return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "scales must be 2-byte aligned");
   const Geometry g{n_sel_blocks, block_tokens, query_heads, kv_heads, head_dim, bits, group_size};
   int st = make_plan(g, aligned16(packed_k) && aligned16(packed_v),
-                     aligned16(scales_k) && aligned16(scales_v), p);
+                     aligned16(scales_k) && aligned16(scales_v), p,
+                     static_cast<long long>(n_pool_blocks) * block_tokens);
   if (st) return st;
   if (!workspace || workspace_bytes < p.ws_bytes)
     return fail(KVSSD_B200_ERR_WORKSPACE, "workspace needs " + std::to_string(p.ws_bytes) + " bytes");
@@ -398,6 +425,17 @@ cudaError_t ensure_dynamic_smem(DecodeKernel kernel, size_t bytes) {
 }
 
 int launch_split(DecodeArgs& a, const Plan& p, cudaStream_t s) {
+  if (p.tma) {
+    // TMA-fed streaming kernel: programmatic stream serialization, cooperative with the fused
+    // combine (as below).
+    cudaError_t e = launch_tma_decode(a, p.n_splits, s);
+    if (e == cudaErrorCooperativeLaunchTooLarge && a.fuse_combine) {
+      cudaGetLastError();
+      a.fuse_combine = 0;
+      return KVSSD_B200_ERR_UNSUPPORTED;
+    }
+    return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "TMA decode launch");
+  }
   {
     cudaError_t e = ensure_dynamic_smem(p.kernel, p.smem);
     if (e != cudaSuccess) return cuda_fail(e, "shared-memory attribute");
@@ -751,7 +789,7 @@ int plan_batched(int n_problems, int block_tokens, int query_heads, int kv_heads
   p.gqa = query_heads / kv_heads;
   p.n_qsub = (p.gqa + 7) / 8;
   p.n_vheads = kv_heads * p.n_qsub;
-  if (!plan_streaming(g, info, p))
+  if (!plan_streaming(g, info, p, false, 0))
     return fail(KVSSD_B200_ERR_UNSUPPORTED,
                 "batched decode needs the streaming kernel's shapes (INT4, head_dim 128, group "
                 "32 or 64, KV heads dividing 16, at most 8 query heads per KV head)");

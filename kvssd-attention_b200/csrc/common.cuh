@@ -32,6 +32,7 @@ enum DeviceStatusBits : unsigned {
   kDevCombineTimeout = 4u,  // a fused combine gave up waiting for the other CTAs' parts
   kDevExchangeTimeout = 8u,  // a cross-GPU exchange gave up waiting for another rank's slice
   kDevBadProblem = 16u,      // a batched problem descriptor was refused (misaligned/invalid)
+  kDevStreamTimeout = 32u,   // a TMA-fed kernel gave up waiting for its copies or ring slots
 };
 
 // The G FP16 scales of one (token, KV head) row, loaded as one 8- or 4-byte word.
@@ -46,6 +47,12 @@ struct ScaleRow {
       const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
       memcpy(s, &w, 4);
     }
+  }
+  // Scales 2i and 2i + 1 as one FP16 pair (low half = scale 2i).
+  __device__ __forceinline__ uint32_t word(int i) const {
+    uint32_t w;
+    memcpy(&w, s + 2 * i, 4);
+    return w;
   }
 };
 
@@ -121,6 +128,16 @@ struct LanePairs<4> {
   }
 };
 
+// Uncentred INT4 pairs: even code slots as FP16 1024 + n, odd slots as 1024 + 16n (one LOP3
+// each); consumers fold the 1/16 and the offsets (1032, 1152) into their other operand.
+__device__ __forceinline__ void raw_pairs4(uint32_t x, uint32_t (&o)[4]) {
+  const uint32_t x8 = x >> 8;
+  o[0] = or_magic<0x000F000Fu>(x);
+  o[1] = or_magic<0x00F000F0u>(x);
+  o[2] = or_magic<0x000F000Fu>(x8);
+  o[3] = or_magic<0x00F000F0u>(x8);
+}
+
 template <>
 struct LanePairs<2> {
   static constexpr int kPairs = 8;
@@ -195,6 +212,13 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint3
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
+}
+
+// GPU-wide nanosecond clock (%globaltimer), the time base of every bounded wait.
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {

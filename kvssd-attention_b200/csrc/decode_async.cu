@@ -36,25 +36,15 @@
 // The CTA finally merges the wph warps of each head through shared memory and writes one
 // (m, l, acc) part per query head; with the fused combine the last CTAs to finish then fold
 // the parts into the output (otherwise the combine kernel does).
-#include "decode_tc.cuh"
 #include "fused_tail.cuh"
+#include "stream_math.cuh"
 
 namespace kvb {
 
-constexpr int kAsyncWarps = 16;
+constexpr int kAsyncWarps = kStreamWarps;
 constexpr int kAsyncThreads = 32 * kAsyncWarps;
 constexpr int kAsyncDepth = 2;  // ring stages per warp (compile-time: cp.async.wait_group N)
 
-
-// D = A * B (zero accumulator start).
-__device__ __forceinline__ void mma_16816_zero(float (&d)[4], uint32_t a0, uint32_t a1,
-                                               uint32_t a2, uint32_t a3, uint32_t b0,
-                                               uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
-}
 
 // Copy side of one warp: the addresses of its next tile and the cursor over the selection.
 // Consecutive tiles of a warp inside one block are 16 * WPH rows apart, so inside a block the
@@ -192,29 +182,9 @@ __device__ __forceinline__ void async_decode_body(const DecodeArgs& a) {
 
   // ---------------- compute state
   const int q0 = h * a.gqa, nq = a.gqa;
-  // Q (pre-multiplied by sm_scale*log2(e)) as the B operand: k-step (m, j2) of thread c covers
-  // dims 32m + 8c + {2j2, 2j2+4} (b0, even code slots) and 32m + 8c + {2j2+1, 2j2+5} (b1, odd
-  // code slots), the order in which the unpacker emits a 32-bit word's codes.
-  uint32_t qf[4][2][2];
-#pragma unroll
-  for (int m = 0; m < 4; ++m)
-#pragma unroll
-    for (int j2 = 0; j2 < 2; ++j2)
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int d0 = 32 * m + 8 * c + 2 * j2 + r, d1 = d0 + 4;
-        float f0 = 0.f, f1 = 0.f;
-        if (g < nq) {
-          const long long qb = static_cast<long long>(q0 + g) * D;
-          f0 = load_query(a.q, a.q_dtype, qb + d0) * a.score_scale;
-          f1 = load_query(a.q, a.q_dtype, qb + d1) * a.score_scale;
-        }
-        qf[m][j2][r] = h2_as_u32(__floats2half2_rn(f0, f1));
-      }
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-  float acc[MT][4];
-#pragma unroll
-  for (int i = 0; i < MT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  QueryFrags<GROUP> qfr;
+  qfr.load(a, q0, nq, g, c);
+  StreamState state;
   // ldmatrix: lane supplies row (lane & 7) of the matrix for 16-byte chunk (lane >> 3), at its
   // swizzled position; rows 8-15 repeat the pattern 8 rows further.
   const int ld_row = lane & 7, ld_chunk = lane >> 3;
@@ -231,18 +201,8 @@ __device__ __forceinline__ void async_decode_body(const DecodeArgs& a) {
     int rows = 16;
     if (partial & (1u << slot)) rows = tile_rows[warp][slot];
     const uint8_t* sp = ring + (st - ring_s);
-    uint32_t kA[4], kB[4], vA[4], vB[4];
-    ScaleRow<G> sk0, sk1, sv[4];
-    ldsm_x4(st + ld_off, kA[0], kA[1], kA[2], kA[3]);               // K tokens 0-7
-    ldsm_x4(st + ld_off + 8 * PD, kB[0], kB[1], kB[2], kB[3]);      // K tokens 8-15
-    ldsm_x4_trans(st + OFF_V + ld_off, vA[0], vA[1], vA[2], vA[3]);
-    ldsm_x4_trans(st + OFF_V + ld_off + 8 * PD, vB[0], vB[1], vB[2], vB[3]);
-    sk0.load(sp + sk_off);
-    sk1.load(sp + sk_off + 8 * SB);
-    sv[0].load(sp + sv_off);
-    sv[1].load(sp + sv_off + SB);
-    sv[2].load(sp + sv_off + 8 * SB);
-    sv[3].load(sp + sv_off + 9 * SB);
+    TileFrags<G> t;
+    t.template load<SB>(st, st + OFF_V, ld_off, sp + sk_off, sp + sv_off, SB);
     __syncwarp();                   // the stage's data is in registers: refill it
     issue(i + DEPTH, slot, st);     // with the tile DEPTH ahead
     if (++slot == DEPTH) {
@@ -252,137 +212,14 @@ __device__ __forceinline__ void async_decode_body(const DecodeArgs& a) {
       st += STAGE;
     }
     if (rows <= 0) continue;
-
-    // ---- QK per scale group: r4 = sum_group (code - 8) q, then scaled by the K scale
-    float x[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      __half2 p0[4], p1[4];
-      LanePairs<BITS>::centred(kA[m], p0);
-      LanePairs<BITS>::centred(kB[m], p1);
-      float r4[4];
-      mma_16816_zero(r4, h2_as_u32(p0[0]), h2_as_u32(p1[0]), h2_as_u32(p0[1]), h2_as_u32(p1[1]),
-                     qf[m][0][0], qf[m][0][1]);
-      mma_16816(r4, h2_as_u32(p0[2]), h2_as_u32(p1[2]), h2_as_u32(p0[3]), h2_as_u32(p1[3]),
-                qf[m][1][0], qf[m][1][1]);
-      const int gi = (32 * m) / GROUP;
-      const float s0 = __half2float(sk0.s[gi]), s1 = __half2float(sk1.s[gi]);
-      x[0] = fmaf(r4[0], s0, x[0]);
-      x[1] = fmaf(r4[1], s0, x[1]);
-      x[2] = fmaf(r4[2], s1, x[2]);
-      x[3] = fmaf(r4[3], s1, x[3]);
-    }
-    // ---- online softmax in the log2 domain; rows g, g+8 x heads 2c, 2c+1
-    if (rows < 16) {  // rows past the valid count hold stale codes: no weight
-      if (g >= rows) x[0] = x[1] = -INFINITY;
-      if (g + 8 >= rows) x[2] = x[3] = -INFINITY;
-    }
-    // The running max moves only when some score exceeds it by kLazyMax: p stays <= 2^8.
-    const bool up = x[0] > m_run[0] + kLazyMax || x[2] > m_run[0] + kLazyMax ||
-                    x[1] > m_run[1] + kLazyMax || x[3] > m_run[1] + kLazyMax;
-    if (__any_sync(0xffffffffu, up)) {
-      float t0 = fmaxf(x[0], x[2]), t1 = fmaxf(x[1], x[3]);
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
-        t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, o));
-      }
-      const float n0 = fmaxf(m_run[0], t0), n1 = fmaxf(m_run[1], t1);
-      const float al0 = fast_exp2(m_run[0] - n0), al1 = fast_exp2(m_run[1] - n1);
-      l_run[0] *= al0;
-      l_run[1] *= al1;
-#pragma unroll
-      for (int k = 0; k < MT; ++k) {
-        acc[k][0] *= al0;
-        acc[k][1] *= al1;
-        acc[k][2] *= al0;
-        acc[k][3] *= al1;
-      }
-      m_run[0] = n0;
-      m_run[1] = n1;
-    }
-    const float e0 = fast_exp2(x[0] - m_run[0]), e1 = fast_exp2(x[1] - m_run[1]);
-    const float e2 = fast_exp2(x[2] - m_run[0]), e3 = fast_exp2(x[3] - m_run[1]);
-    l_run[0] += e0 + e2;
-    l_run[1] += e1 + e3;
-    const __half2 pt0 = u32_as_h2(transpose_8x8(h2_as_u32(__floats2half2_rn(e0, e1))));
-    const __half2 pt1 = u32_as_h2(transpose_8x8(h2_as_u32(__floats2half2_rn(e2, e3))));
-    // ---- PV per 32-dim chunk j (inside one scale group): P' = P * sv[t, group]
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int gi = (32 * j) / GROUP;
-      const __half2 b0 = __hmul2(pt0, __halves2half2(sv[0].s[gi], sv[1].s[gi]));
-      const __half2 b1 = __hmul2(pt1, __halves2half2(sv[2].s[gi], sv[3].s[gi]));
-      __half2 cA[4], cB[4];
-      LanePairs<BITS>::centred(vA[j], cA);
-      LanePairs<BITS>::centred(vB[j], cB);
-#pragma unroll
-      for (int k2 = 0; k2 < 2; ++k2)
-        mma_16816(acc[2 * j + k2], h2_as_u32(cA[2 * k2]), h2_as_u32(cA[2 * k2 + 1]),
-                  h2_as_u32(cB[2 * k2]), h2_as_u32(cB[2 * k2 + 1]), h2_as_u32(b0),
-                  h2_as_u32(b1));
-    }
+    float x[4];
+    qk_tile<GROUP>(t, qfr, x);
+    softmax_pv_tile<GROUP, false>(x, rows, g, qfr.unscale, t, state);
   }
+  finish_stream<GROUP, false>(state, c);
   cp_async_wait<0>();
   __syncthreads();
-
-  // ---- merge the wph warps of each head through shared memory: [slot][field][lane]
-  constexpr int kFields = 4 + 4 * MT;
-  float* buf = reinterpret_cast<float*>(smem);
-  if (sub > 0) {
-    float* dst = buf + static_cast<size_t>((sub - 1) * KVH + h) * kFields * 32 + lane;
-    dst[0] = m_run[0];
-    dst[32] = m_run[1];
-    dst[64] = l_run[0];
-    dst[96] = l_run[1];
-#pragma unroll
-    for (int k = 0; k < MT; ++k)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) dst[(4 + 4 * k + e) * 32] = acc[k][e];
-  }
-  __syncthreads();
-  if (sub == 0) {
-    for (int o = 1; o < WPH; ++o) {
-      const float* src = buf + static_cast<size_t>((o - 1) * KVH + h) * kFields * 32 + lane;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const float mo = src[hh * 32], lo = src[(2 + hh) * 32];
-        const float mn = fmaxf(m_run[hh], mo);
-        const float a0 = mn == -INFINITY ? 0.f : fast_exp2(m_run[hh] - mn);
-        const float a1 = mn == -INFINITY ? 0.f : fast_exp2(mo - mn);
-        m_run[hh] = mn;
-        l_run[hh] = l_run[hh] * a0 + lo * a1;
-#pragma unroll
-        for (int k = 0; k < MT; ++k) {
-          acc[k][hh] = acc[k][hh] * a0 + src[(4 + 4 * k + hh) * 32] * a1;
-          acc[k][2 + hh] = acc[k][2 + hh] * a0 + src[(4 + 4 * k + 2 + hh) * 32] * a1;
-        }
-      }
-    }
-    // ---- this CTA's part; O^T row g of M-tile (j, k2) is dim 32j + 4g + 2k2, row g+8 the next
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], o);
-      l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], o);
-    }
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int n = 2 * c + hh;
-      if (n >= nq) continue;
-      const size_t row = static_cast<size_t>(blockIdx.x) * a.qh + (q0 + n);
-      if (g == 0) {
-        a.part_ml[row * 2 + 0] = m_run[hh];
-        a.part_ml[row * 2 + 1] = l_run[hh];
-      }
-      float* dst = a.part_acc + row * D + 4 * g;
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int k2 = 0; k2 < 2; ++k2)
-          *reinterpret_cast<float2*>(dst + 32 * j + 2 * k2) =
-              make_float2(acc[2 * j + k2][hh], acc[2 * j + k2][2 + hh]);
-    }
-  }
+  merge_warps_write_part<KVH>(a, reinterpret_cast<float*>(smem), warp, lane, q0, nq, state);
   if (a.fuse_combine) fused_combine_tail<D>(a, epoch, a.n_splits);
 }
 

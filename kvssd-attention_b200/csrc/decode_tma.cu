@@ -1,0 +1,385 @@
+// Streaming split-KV decode fed by TMA (sm_100a): a producer warp copies whole 16-token
+// tile-rows of the selection (K, V and both scale rows of ALL KV heads, one tensor copy each)
+// into a ring of shared-memory stages; the 16 consumer warps only run the tile math.
+//
+// Work split as in the cp.async-fed kernel (decode_async.cu): one CTA per SM owns a contiguous
+// range of 16-token tile-rows of the selection; consumer warp w serves KV head w % kvh and the
+// tile-rows k == w / kvh (mod 16 / kvh), so the 16 / kvh consumer groups interleave tile-rows
+// and each group has its own ring of kTmaSlots stages. A stage holds
+//   K  [kvh][16 rows][64 B]   one 3-D TMA box (dims: bytes, token rows, heads -- the heads are
+//   V  [kvh][16 rows][64 B]   the outer box dimension, so each head's 16 rows are contiguous)
+//   KS [16 rows][kvh * G * 2 B], VS [16 rows][kvh * G * 2 B]   one 2-D box each,
+// all with the TMA's address-based 16-byte-chunk swizzle (64-byte rows: chunk q of row r at
+// q ^ ((r >> 1) & 3), the layout ldmatrix reads without bank conflicts). A tile-row never
+// crosses a block (block_tokens is a multiple of 16); the producer resolves the block through
+// the block table once per 32 blocks (a warp-wide cache) and copies all 16 rows even when fewer
+// are valid (the pool holds whole blocks); the stage's valid row count travels in shared
+// memory. A refused block-table entry gets no copy and a zero row count.
+//
+// Synchronisation: per stage a "full" mbarrier (the producer's arrive with the stage's byte
+// count; the TMA completes the bytes) and an "empty" mbarrier (one arrive per consumer warp of
+// the group, after its QK MMAs have consumed the tile's last shared-memory loads). Each
+// consumer group has its own producer warp (warp 16 + group), which blocks on its ring's next
+// empty barrier: no group waits behind another, and a waiting producer takes no issue slots.
+// Every wait is bounded (about a second, and a poll count): on timeout the kernel flags
+// kDevStreamTimeout, waits (bounded) for the copies it issued, and finishes with what it has.
+#include <cuda.h>
+
+#include <mutex>
+#include <vector>
+
+#include "fused_tail.cuh"
+#include "stream_math.cuh"
+#include "tma.cuh"
+
+namespace kvb {
+
+struct TmaMaps {
+  CUtensorMap k, v, ks, vs;
+};
+
+constexpr int kTmaSlots = 4;  // ring stages per consumer group
+constexpr uint32_t kTmaMaxPolls = 1u << 26;
+
+template <int KVH, int G>
+struct TmaLayout {
+  static constexpr int WPH = kStreamWarps / KVH;  // consumer groups = producer warps
+  static constexpr int THREADS = 32 * (kStreamWarps + WPH);
+  static constexpr int NS = WPH * kTmaSlots;      // ring stages
+  static constexpr int SRB = KVH * 2 * G;         // scale bytes per token row
+  static constexpr int KV_BYTES = 16 * KVH * 64;  // K (or V) bytes per stage
+  static constexpr int S_BYTES = 16 * SRB;        // K (or V) scale bytes per stage
+  static constexpr int S_SPAN = (S_BYTES + 1023) / 1024 * 1024;
+  static constexpr int OFF_V = KV_BYTES, OFF_KS = 2 * KV_BYTES, OFF_VS = OFF_KS + S_SPAN;
+  static constexpr int STAGE = OFF_VS + S_SPAN;   // multiple of 1024: swizzle phase = address
+  static constexpr uint32_t TX = 2 * KV_BYTES + 2 * S_BYTES;
+  // Scale rows use the TMA swizzle whose span equals the row (16 B rows: none).
+  static constexpr uint32_t SWZ = SRB >= 128 ? 7u : SRB == 64 ? 3u : SRB == 32 ? 1u : 0u;
+  static constexpr size_t SMEM = 1024 + static_cast<size_t>(NS) * STAGE;  // + alignment slack
+  __device__ static uint32_t swizzled(uint32_t off) { return off ^ (((off >> 7) & SWZ) << 4); }
+};
+
+template <int KVH, int GROUP>
+__global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP>::THREADS, 1)
+    tma_decode_kernel(const DecodeArgs a, const __grid_constant__ TmaMaps maps) {
+  constexpr int D = 128, G = D / GROUP;
+  using L = TmaLayout<KVH, G>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full[L::NS], empty[L::NS];
+  __shared__ int stage_rows[L::NS];
+  const uint32_t raw_s = smem_addr(smem_raw);
+  const uint32_t ring_s = (raw_s + 1023u) & ~1023u;
+  uint8_t* ring = smem_raw + (ring_s - raw_s);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int h = warp % KVH, grp = warp / KVH;
+  // Programmatic stream serialization: wait for the preceding grid before the first global
+  // access, and let the next launch start early.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
+  const unsigned epoch =
+      a.xworld ? *reinterpret_cast<const volatile unsigned*>(a.xpeers[a.xrank]) + 1u : 0u;
+  const unsigned long long deadline = global_ns() + kCombineWaitNs;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < L::NS; ++s) {
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&empty[s]), KVH);
+    }
+    mbar_init_fence();
+  }
+  __syncthreads();
+
+  const long long t_begin = a.total_tiles * blockIdx.x / a.n_splits;
+  const int n_tiles = static_cast<int>(a.total_tiles * (blockIdx.x + 1) / a.n_splits - t_begin);
+  int issued = 0;  // producer: stages issued to its group
+  StreamState state;
+  const int q0 = h * a.gqa, nq = a.gqa;
+
+  if (warp >= kStreamWarps) {
+    // ---------------- producer of group gp
+    const int gp = warp - kStreamWarps;
+    if (lane == 0) {
+      prefetch_tensor_map(&maps.k);
+      prefetch_tensor_map(&maps.v);
+      prefetch_tensor_map(&maps.ks);
+      prefetch_tensor_map(&maps.vs);
+    }
+    const uint64_t policy = l2_evict_first();
+    BlockInfoCache cache;
+#pragma unroll 1
+    for (int k = gp; k < n_tiles; k += L::WPH, ++issued) {
+      const int sl = gp * kTmaSlots + issued % kTmaSlots;
+      const bool free_slot = mbar_wait_until(smem_addr(&empty[sl]),
+                                             ((issued / kTmaSlots) & 1) ^ 1, deadline,
+                                             kTmaMaxPolls);
+      if (!__all_sync(0xffffffffu, free_slot)) {  // the warp leaves together
+        if (lane == 0) atomicOr(a.status, kDevStreamTimeout);
+        break;
+      }
+      const long long t = t_begin + k;
+      const int slot = static_cast<int>(t / a.tiles_per_block);
+      const int tib = static_cast<int>(t - static_cast<long long>(slot) * a.tiles_per_block);
+      int blk, valid;
+      cache.lookup(a, slot, lane, blk, valid);
+      const int rows = blk < 0 ? 0 : min(16, valid - 16 * tib);
+      if (lane == 0) {
+        stage_rows[sl] = rows;
+        const uint32_t bar = smem_addr(&full[sl]);
+        if (rows > 0) {
+          const uint32_t st = ring_s + sl * L::STAGE;
+          const int row0 = blk * a.bt + 16 * tib;
+          mbar_arrive_expect_tx(bar, L::TX);
+          tma_load_3d(st, &maps.k, 0, row0, 0, bar, policy);
+          tma_load_3d(st + L::OFF_V, &maps.v, 0, row0, 0, bar, policy);
+          tma_load_2d(st + L::OFF_KS, &maps.ks, 0, row0, bar, policy);
+          tma_load_2d(st + L::OFF_VS, &maps.vs, 0, row0, bar, policy);
+        } else {
+          mbar_arrive(bar);  // nothing to copy: the stage is complete at once
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    // ---------------- consumers
+    QueryFrags<GROUP> qfr;
+    qfr.load(a, q0, nq, g, c);
+    const int ld_row = lane & 7, ld_chunk = lane >> 3;
+    const uint32_t ld_off =
+        static_cast<uint32_t>(ld_row * 64 + ((ld_chunk ^ ((ld_row >> 1) & 3)) << 4));
+    const uint32_t hs = static_cast<uint32_t>(h * 2 * G);  // head's byte offset in a scale row
+    const uint32_t sk_off = L::swizzled(g * L::SRB + hs);
+    const uint32_t sv_off = L::swizzled(2 * c * L::SRB + hs);
+    const int sv_odd = static_cast<int>(L::swizzled((2 * c + 1) * L::SRB + hs)) -
+                       static_cast<int>(sv_off);
+    const int n_mine = grp < n_tiles ? (n_tiles - grp + L::WPH - 1) / L::WPH : 0;
+#pragma unroll 1
+    for (int i = 0; i < n_mine; ++i) {
+      const int sl = grp * kTmaSlots + i % kTmaSlots;
+      const bool landed =
+          mbar_wait_until(smem_addr(&full[sl]), (i / kTmaSlots) & 1, deadline, kTmaMaxPolls);
+      if (!__all_sync(0xffffffffu, landed)) {  // the warp leaves together
+        if (lane == 0) atomicOr(a.status, kDevStreamTimeout);
+        break;
+      }
+      const int rows = stage_rows[sl];
+      const uint32_t empty_bar = smem_addr(&empty[sl]);
+      if (rows <= 0) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar);
+        continue;
+      }
+      const uint32_t st = ring_s + sl * L::STAGE;
+      const uint8_t* sp = ring + sl * L::STAGE;
+      TileFrags<G> t;
+      t.template load<L::SRB>(st + h * 1024, st + L::OFF_V + h * 1024, ld_off,
+                              sp + L::OFF_KS + sk_off, sp + L::OFF_VS + sv_off, sv_odd);
+      float x[4];
+      qk_tile<GROUP>(t, qfr, x);
+      __syncwarp();  // every lane's loads of the stage have been consumed: release it
+      if (lane == 0) mbar_arrive(empty_bar);
+      softmax_pv_tile<GROUP, true>(x, rows, g, qfr.unscale, t, state);
+    }
+    finish_stream<GROUP, true>(state, c);
+  }
+  __syncthreads();
+  if (warp >= kStreamWarps && lane == 0) {
+    // Copies still in flight can only be the group's last kTmaSlots stages (after a timeout);
+    // wait for them (bounded) before the ring is reused and the CTA exits.
+    const int gp = warp - kStreamWarps;
+    const unsigned long long drain_deadline = global_ns() + kCombineWaitNs;
+    for (int idx = max(0, issued - kTmaSlots); idx < issued; ++idx)
+      if (!mbar_wait_until(smem_addr(&full[gp * kTmaSlots + idx % kTmaSlots]),
+                           (idx / kTmaSlots) & 1, drain_deadline, kTmaMaxPolls))
+        atomicOr(a.status, kDevStreamTimeout);
+  }
+  __syncthreads();
+  merge_warps_write_part<KVH>(a, reinterpret_cast<float*>(ring), warp, lane, q0, nq, state);
+  if (a.fuse_combine) fused_combine_tail<D>(a, epoch, a.n_splits);
+}
+
+using TmaKernel = void (*)(const DecodeArgs, const TmaMaps);
+
+template <int GROUP>
+TmaKernel tma_kernel_for_heads(int kvh) {
+  switch (kvh) {
+    case 4: return tma_decode_kernel<4, GROUP>;
+    case 8: return tma_decode_kernel<8, GROUP>;
+    case 16: return tma_decode_kernel<16, GROUP>;
+    default: return nullptr;
+  }
+}
+
+TmaKernel tma_kernel_for(int bits, int d, int group, int kvh) {
+  if (bits != 4 || d != 128) return nullptr;
+  switch (group) {
+    case 32: return tma_kernel_for_heads<32>(kvh);
+    case 64: return tma_kernel_for_heads<64>(kvh);
+    default: return nullptr;
+  }
+}
+
+template <int G>
+int tma_threads_for_heads(int kvh) {
+  switch (kvh) {
+    case 4: return TmaLayout<4, G>::THREADS;
+    case 8: return TmaLayout<8, G>::THREADS;
+    case 16: return TmaLayout<16, G>::THREADS;
+    default: return 0;
+  }
+}
+
+template <int G>
+size_t tma_smem_for_heads(int kvh) {
+  switch (kvh) {
+    case 4: return TmaLayout<4, G>::SMEM;
+    case 8: return TmaLayout<8, G>::SMEM;
+    case 16: return TmaLayout<16, G>::SMEM;
+    default: return 0;
+  }
+}
+
+// ---------------- host side
+
+// Tensor-map encoder from the driver (resolved once through the runtime; no libcuda link).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn tensor_map_encoder() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Encoded maps are cached by (kind, pointer, rows, row bytes): a decode loop over the same
+// pools encodes once.
+struct MapKey {
+  int kind;
+  const void* ptr;
+  unsigned long long rows;
+  int row_bytes;
+  bool operator==(const MapKey& o) const {
+    return kind == o.kind && ptr == o.ptr && rows == o.rows && row_bytes == o.row_bytes;
+  }
+};
+
+bool encode_cached(const MapKey& key, CUtensorMap* out) {
+  static std::mutex mu;
+  static std::vector<std::pair<MapKey, CUtensorMap>> cache;
+  static size_t next_victim = 0;
+  constexpr size_t kCapacity = 256;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& e : cache)
+    if (e.first == key) {
+      *out = e.second;
+      return true;
+    }
+  EncodeTiledFn enc = tensor_map_encoder();
+  if (!enc) return false;
+  CUtensorMap m;
+  CUresult r;
+  if (key.kind < 2) {
+    // K or V codes: (64 bytes, token rows, heads) with strides (heads * 64, 64); box
+    // {64, 16, heads} lands as [head][row][64 B] with the 64-byte swizzle.
+    const int heads = key.row_bytes / 64;
+    const cuuint64_t dims[3] = {64, key.rows, static_cast<cuuint64_t>(heads)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(key.row_bytes), 64};
+    const cuuint32_t box[3] = {64, 16, static_cast<cuuint32_t>(heads)};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(key.ptr), dims, strides, box,
+            elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    // K or V scale rows: (row bytes, token rows); box {row bytes, 16}.
+    const int rb = key.row_bytes;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(rb), key.rows};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(rb)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(rb), 16};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUtensorMapSwizzle swz = rb >= 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                   : rb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                   : rb == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                              : CU_TENSOR_MAP_SWIZZLE_NONE;
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(key.ptr), dims, strides, box,
+            elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  if (r != CUDA_SUCCESS) return false;
+  if (cache.size() < kCapacity) {
+    cache.emplace_back(key, m);
+  } else {
+    cache[next_victim] = {key, m};
+    next_victim = (next_victim + 1) % kCapacity;
+  }
+  *out = m;
+  return true;
+}
+
+bool tma_decode_supported(int bits, int d, int group, int kvh, int bt) {
+  return tma_kernel_for(bits, d, group, kvh) != nullptr && bt % 16 == 0 &&
+         tensor_map_encoder() != nullptr;
+}
+
+size_t tma_decode_smem(int kvh, int group) {
+  return group == 32 ? tma_smem_for_heads<4>(kvh) : tma_smem_for_heads<2>(kvh);
+}
+
+int tma_decode_threads(int kvh, int group) {
+  return group == 32 ? tma_threads_for_heads<4>(kvh) : tma_threads_for_heads<2>(kvh);
+}
+
+// Launches the TMA-fed decode over grid (n_splits, 1): cooperative when the fused combine is
+// on. Returns cudaErrorInvalidValue if the tensor maps cannot be encoded.
+cudaError_t launch_tma_decode(const DecodeArgs& a, int n_splits, cudaStream_t s) {
+  const TmaKernel kernel = tma_kernel_for(a.bits, a.d, a.group, a.kvh);
+  if (!kernel) return cudaErrorInvalidValue;
+  const size_t smem = tma_decode_smem(a.kvh, a.group);
+  {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static std::mutex mu;
+    static std::vector<std::pair<int, const void*>> done;
+    std::lock_guard<std::mutex> lock(mu);
+    const std::pair<int, const void*> key{dev, reinterpret_cast<const void*>(kernel)};
+    bool set = false;
+    for (const auto& d : done) set = set || d == key;
+    if (!set) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      done.push_back(key);
+    }
+  }
+  const unsigned long long rows = static_cast<unsigned long long>(a.n_pool) * a.bt;
+  const int srb = a.kvh * 2 * (a.d / a.group);
+  TmaMaps maps;
+  if (!encode_cached({0, a.kp, rows, a.kvh * 64}, &maps.k) ||
+      !encode_cached({1, a.vp, rows, a.kvh * 64}, &maps.v) ||
+      !encode_cached({2, a.ks, rows, srb}, &maps.ks) ||
+      !encode_cached({3, a.vs, rows, srb}, &maps.vs))
+    return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_splits, 1, 1);
+  cfg.blockDim = dim3(tma_decode_threads(a.kvh, a.group), 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.fuse_combine ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, a, maps);
+}
+
+}  // namespace kvb

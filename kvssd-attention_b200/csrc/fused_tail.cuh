@@ -13,12 +13,6 @@ namespace kvb {
 constexpr unsigned long long kCombineWaitNs = 1000000000ull;
 constexpr unsigned kCombineMaxPolls = 1u << 26;
 
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
 // Cross-GPU exchange of one combined slice, run by warp 0 of the CTA that combined it (token-
 // range shards of one context, one rank per GPU). Every value travels as one 64-bit word
 // {value, epoch} written with a single store into buffer half (epoch & 1) of every rank's

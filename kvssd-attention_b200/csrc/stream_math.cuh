@@ -1,0 +1,393 @@
+// Per-warp tile math of the streaming decode kernels (INT4 codes, head_dim 128, group 32 or
+// 64): one warp serves one KV head and up to 8 of its query heads, and consumes 16-token tiles
+// whose K and V rows (64 bytes per token) sit in shared memory with 16-byte chunk q of row r
+// stored at chunk q ^ ((r >> 1) & 3), plus the tile's FP16 scale rows. The kernels differ only
+// in how tiles reach shared memory (decode_async.cu: per-warp cp.async rings; decode_tma.cu:
+// TMA copies into a CTA ring).
+//
+//   QK: S[t,n] = sum_group sk[t,group] * (sum_{d in group} (code-8)[t,d] * q[n,d]). The codes
+//       enter the MMAs uncentred (even code slots as FP16 1024 + n, odd slots 1024 + 16n; one
+//       LOP3 each), the odd slots' q is divided by 16, and the constant part -- per (scale
+//       group, query head) Qg = sum 1032 q_even + 1152 q_odd/16 -- is subtracted by one more
+//       MMA per tile whose A operand is the tile's K scale rows (the accumulator starts at
+//       -sk x Qg). q is scaled by a per-warp power of two qs so |q| < 4 (Qg stays inside FP16
+//       range); scores come out divided by qs and the softmax multiplies by 1/qs (exact).
+//   PV: O^T[d,n] = sum_t (code-8)[t,d] * (P[t,n] * sv[t,group(d)]); the V scale is folded into
+//       the FP16 P operand (P') of the M-tiles of that group; ldmatrix.trans delivers V with two
+//       tokens per 32-bit register, the pairing the PV A fragment needs. Two forms of the V
+//       codes (template flag VRAW; each feed is fastest with one of them, measured): centred
+//       FP16 values (one LOP3 + one HSUB2/HFMA2 per pair), or -- VRAW -- the codes enter the
+//       MMAs uncentred as exact FP16 subnormals (even code slots n * 2^-24, odd slots
+//       n * 2^-20; one AND each), so the accumulator holds sum n P' scaled by 2^-24 / 2^-20;
+//       the offset 8 * sum_t P' per (query head, scale group) is tracked by one more MMA per
+//       tile, S += P^T sv (A = the transposed P the PV step already has, B = the tile's V scale
+//       rows), and removed once per warp at the end (finish_stream). S sums the unrounded
+//       products P sv rather than the FP16 P', which adds at most 8 x the FP16 rounding of P'
+//       -- the same order as the rounding of P' itself.
+//   Online softmax in the log2 domain (q pre-scaled by sm_scale * log2 e) with a lazily
+//   updated running max: the max and the accumulator move only when a score exceeds the
+//   running max by 2^8, detected with one warp vote per tile.
+#pragma once
+
+#include "decode_tc.cuh"
+
+namespace kvb {
+
+constexpr int kStreamWarps = 16;  // consumer warps of a streaming CTA (warp w: KV head w % kvh)
+
+// D = A * B (zero accumulator start).
+__device__ __forceinline__ void mma_16816_zero(float (&d)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+// The B operands of one warp's QK MMAs and the K offset constants.
+template <int GROUP>
+struct QueryFrags {
+  static constexpr int D = 128, G = D / GROUP;
+  // k-step (m, j2) of thread c covers dims 32m + 8c + {2j2, 2j2+4} (b0, even code slots) and
+  // 32m + 8c + {2j2+1, 2j2+5} (b1, odd code slots), the order in which a word's codes unpack.
+  uint32_t qf[4][2][2];
+  uint32_t qb[2];  // -Qg split over the four k-slices of the offset MMA (B operand)
+  float unscale;   // 1 / qs
+
+  // Query heads q0 .. q0 + nq - 1 (nq <= 8) of this warp; thread (g, c) holds head g's q.
+  __device__ __forceinline__ void load(const DecodeArgs& a, int q0, int nq, int g, int c) {
+    float qv[4][2][2][2];  // [m][j2][r][dim d0 / d1], all loaded before any is used
+    float qmax = 0.f;
+#pragma unroll
+    for (int m = 0; m < 4; ++m)
+#pragma unroll
+      for (int j2 = 0; j2 < 2; ++j2)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int d0 = 32 * m + 8 * c + 2 * j2 + r, d1 = d0 + 4;
+          qv[m][j2][r][0] = qv[m][j2][r][1] = 0.f;
+          if (g < nq) {
+            const long long base = static_cast<long long>(q0 + g) * D;
+            qv[m][j2][r][0] = load_query(a.q, a.q_dtype, base + d0) * a.score_scale;
+            qv[m][j2][r][1] = load_query(a.q, a.q_dtype, base + d1) * a.score_scale;
+          }
+          qmax = fmaxf(qmax, fmaxf(fabsf(qv[m][j2][r][0]), fabsf(qv[m][j2][r][1])));
+        }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, o));
+    const int qexp = (__float_as_uint(qmax) >> 23) & 0xff;
+    // qmax * qs in [2, 4); qs = 1 for a zero or tiny query (and for non-finite ones).
+    const float qs = (qexp >= 2 && qexp <= 253) ? __uint_as_float((255u - qexp) << 23) : 1.f;
+    unscale = 1.f / qs;
+    float qsum[4];  // this thread's share of chunk m's offset for query head g
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      qsum[m] = 0.f;
+#pragma unroll
+      for (int j2 = 0; j2 < 2; ++j2)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const float sc = qs * (r ? 0.0625f : 1.f);
+          const __half2 hq = __floats2half2_rn(qv[m][j2][r][0] * sc, qv[m][j2][r][1] * sc);
+          qf[m][j2][r] = h2_as_u32(hq);
+          qsum[m] += (r ? 1152.f : 1032.f) * (__low2float(hq) + __high2float(hq));
+        }
+      qsum[m] += __shfl_xor_sync(0xffffffffu, qsum[m], 1);
+      qsum[m] += __shfl_xor_sync(0xffffffffu, qsum[m], 2);
+    }
+    // Qg per scale group in two FP16 parts: hi = fp16(Qg / 2) from threads c = 0, 1, the
+    // remainder Qg - 2 hi from c = 2, nothing from c = 3 (|Qg| < 2^17: no part overflows, and
+    // the pair keeps ~22 bits of Qg).
+    __half part[4];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi) {
+      float qg = 0.f;
+#pragma unroll
+      for (int m = 0; m < 4; ++m)
+        if ((32 * m) / GROUP == gi) qg += qsum[m];
+      const __half hi = __float2half_rn(0.5f * qg);
+      const __half lo = __float2half_rn(qg - 2.f * __half2float(hi));
+      part[gi] = __hneg(c < 2 ? hi : c == 2 ? lo : __float2half_rn(0.f));
+    }
+    qb[0] = h2_as_u32(__halves2half2(part[0], part[1]));
+    qb[1] = G == 4 ? h2_as_u32(__halves2half2(part[2], part[3])) : 0u;
+  }
+};
+
+// One tile's operands in registers: K and V fragments of rows 0-7 (A) and 8-15 (B), the K scale
+// rows of tokens g and g + 8 and the V scale rows of tokens 2c, 2c+1, 2c+8, 2c+9.
+template <int G>
+struct TileFrags {
+  uint32_t kA[4], kB[4], vA[4], vB[4];
+  ScaleRow<G> sk0, sk1, sv[4];
+
+  // k_tile / v_tile: shared address of row 0 of the head's 16-row K / V tile (64-byte rows,
+  // 512-byte aligned so the chunk swizzle is address-based); ld_off: this lane's ldmatrix
+  // offset; sk / sv: generic pointers to the K scale row of token g and the V scale row of
+  // token 2c; srow: bytes between consecutive scale rows; sv_odd: offset of token 2c + 1's V
+  // scale row from token 2c's. The V fragments and scales are loaded before the K ones, so
+  // once the QK MMAs have consumed K every shared-memory read of the tile has completed.
+  template <int SROW>
+  __device__ __forceinline__ void load(uint32_t k_tile, uint32_t v_tile, uint32_t ld_off,
+                                       const uint8_t* sk, const uint8_t* sv_row, int sv_odd) {
+    ldsm_x4_trans(v_tile + ld_off, vA[0], vA[1], vA[2], vA[3]);
+    ldsm_x4_trans(v_tile + ld_off + 8 * 64, vB[0], vB[1], vB[2], vB[3]);
+    sv[0].load(sv_row);
+    sv[1].load(sv_row + sv_odd);
+    sv[2].load(sv_row + 8 * SROW);
+    sv[3].load(sv_row + 8 * SROW + sv_odd);
+    sk0.load(sk);
+    sk1.load(sk + 8 * SROW);
+    ldsm_x4(k_tile + ld_off, kA[0], kA[1], kA[2], kA[3]);            // K tokens 0-7
+    ldsm_x4(k_tile + ld_off + 8 * 64, kB[0], kB[1], kB[2], kB[3]);   // K tokens 8-15
+  }
+};
+
+// Scale gi of a scale row as FP32, read straight from its 32-bit word (one conversion).
+template <int G>
+__device__ __forceinline__ float scale_f32(const ScaleRow<G>& r, int gi) {
+  const __half2 w = u32_as_h2(r.word(gi >> 1));
+  return (gi & 1) ? __high2float(w) : __low2float(w);
+}
+
+// (scale gi of row a, scale gi of row b) as one FP16 pair: one byte permute of the two words.
+template <int G>
+__device__ __forceinline__ __half2 scale_pair(const ScaleRow<G>& a, const ScaleRow<G>& b, int gi) {
+  return u32_as_h2(__byte_perm(a.word(gi >> 1), b.word(gi >> 1), (gi & 1) ? 0x7632u : 0x5410u));
+}
+
+// Uncentred INT4 pairs as FP16 subnormals: even code slots n * 2^-24, odd slots 16n * 2^-24
+// (one AND each).
+__device__ __forceinline__ void subnormal_pairs4(uint32_t x, uint32_t (&o)[4]) {
+  const uint32_t x8 = x >> 8;
+  o[0] = x & 0x000F000Fu;
+  o[1] = x & 0x00F000F0u;
+  o[2] = x8 & 0x000F000Fu;
+  o[3] = x8 & 0x00F000F0u;
+}
+
+struct StreamState {
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  float acc[8][4];  // PV accumulators, uncentred and scaled (see finish_stream)
+  float vs[4];      // S = sum_t P[t, head g] sv[t, group 2c + e] in vs[e] (e = 0, 1)
+  __device__ __forceinline__ StreamState() {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    vs[0] = vs[1] = vs[2] = vs[3] = 0.f;
+  }
+};
+
+// Scores of one tile (divided by qs): rows g, g+8 x heads 2c, 2c+1.
+template <int GROUP>
+__device__ __forceinline__ void qk_tile(const TileFrags<128 / GROUP>& t, const QueryFrags<GROUP>& q,
+                                        float (&x)[4]) {
+  constexpr int G = 128 / GROUP;
+  mma_16816_zero(x, t.sk0.word(0), t.sk1.word(0), t.sk0.word(G == 4 ? 1 : 0),
+                 t.sk1.word(G == 4 ? 1 : 0), q.qb[0], q.qb[1]);
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    uint32_t p0[4], p1[4];
+    raw_pairs4(t.kA[m], p0);
+    raw_pairs4(t.kB[m], p1);
+    float r4[4];
+    mma_16816_zero(r4, p0[0], p1[0], p0[1], p1[1], q.qf[m][0][0], q.qf[m][0][1]);
+    mma_16816(r4, p0[2], p1[2], p0[3], p1[3], q.qf[m][1][0], q.qf[m][1][1]);
+    const int gi = (32 * m) / GROUP;
+    const float s0 = scale_f32(t.sk0, gi), s1 = scale_f32(t.sk1, gi);
+    x[0] = fmaf(r4[0], s0, x[0]);
+    x[1] = fmaf(r4[1], s0, x[1]);
+    x[2] = fmaf(r4[2], s1, x[2]);
+    x[3] = fmaf(r4[3], s1, x[3]);
+  }
+}
+
+// Online softmax of one tile's scores and the PV accumulation. rows: valid rows of the tile
+// (rows past it hold stale codes and get no weight). VRAW: subnormal V codes plus the S MMA.
+template <int GROUP, bool VRAW>
+__device__ __forceinline__ void softmax_pv_tile(float (&x)[4], int rows, int g, float unscale,
+                                                const TileFrags<128 / GROUP>& t,
+                                                StreamState& s) {
+  constexpr float kLazyMax = 8.f;  // rescale only when a score beats the running max by 2^8
+  if (rows < 16) {
+    if (g >= rows) x[0] = x[1] = -INFINITY;
+    if (g + 8 >= rows) x[2] = x[3] = -INFINITY;
+  }
+  // Scores relative to the running max: dx = x / qs - m.
+  float dx[4] = {fmaf(x[0], unscale, -s.m_run[0]), fmaf(x[1], unscale, -s.m_run[1]),
+                 fmaf(x[2], unscale, -s.m_run[0]), fmaf(x[3], unscale, -s.m_run[1])};
+  const bool up = dx[0] > kLazyMax || dx[2] > kLazyMax || dx[1] > kLazyMax || dx[3] > kLazyMax;
+  if (__any_sync(0xffffffffu, up)) {
+    float t0 = fmaxf(x[0], x[2]), t1 = fmaxf(x[1], x[3]);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
+      t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, o));
+    }
+    const float n0 = fmaxf(s.m_run[0], t0 * unscale), n1 = fmaxf(s.m_run[1], t1 * unscale);
+    const float al0 = fast_exp2(s.m_run[0] - n0), al1 = fast_exp2(s.m_run[1] - n1);
+    s.l_run[0] *= al0;
+    s.l_run[1] *= al1;
+    // S rows are query heads: head g's factor is al0 / al1 of the lanes with c = g / 2.
+    const float a0g = __shfl_sync(0xffffffffu, al0, g >> 1);
+    const float a1g = __shfl_sync(0xffffffffu, al1, g >> 1);
+    const float alg = (g & 1) ? a1g : a0g;
+    if (VRAW) {
+      s.vs[0] *= alg;
+      s.vs[1] *= alg;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      s.acc[k][0] *= al0;
+      s.acc[k][1] *= al1;
+      s.acc[k][2] *= al0;
+      s.acc[k][3] *= al1;
+    }
+    s.m_run[0] = n0;
+    s.m_run[1] = n1;
+    dx[0] = fmaf(x[0], unscale, -n0);
+    dx[1] = fmaf(x[1], unscale, -n1);
+    dx[2] = fmaf(x[2], unscale, -n0);
+    dx[3] = fmaf(x[3], unscale, -n1);
+  }
+  const float e0 = fast_exp2(dx[0]), e1 = fast_exp2(dx[1]);
+  const float e2 = fast_exp2(dx[2]), e3 = fast_exp2(dx[3]);
+  s.l_run[0] += e0 + e2;
+  s.l_run[1] += e1 + e3;
+  const __half2 pt0 = u32_as_h2(transpose_8x8(h2_as_u32(__floats2half2_rn(e0, e1))));
+  const __half2 pt1 = u32_as_h2(transpose_8x8(h2_as_u32(__floats2half2_rn(e2, e3))));
+  // S += P^T sv: A rows = query heads (pt0 / pt1 hold tokens 2c, 2c+1 / 2c+8, 2c+9 of head g),
+  // B columns = scale groups (thread (g, c) supplies group g's scales of those tokens).
+  if (VRAW) {
+    constexpr int G = 128 / GROUP;
+    const int gs = g & (G - 1);
+    const uint32_t sel = (gs & 1) ? 0x7632u : 0x5410u;
+    const bool hi = G == 4 && (gs & 2);
+    const uint32_t b0 = __byte_perm(hi ? t.sv[0].word(1) : t.sv[0].word(0),
+                                    hi ? t.sv[1].word(1) : t.sv[1].word(0), sel);
+    const uint32_t b1 = __byte_perm(hi ? t.sv[2].word(1) : t.sv[2].word(0),
+                                    hi ? t.sv[3].word(1) : t.sv[3].word(0), sel);
+    mma_16816(s.vs, h2_as_u32(pt0), 0u, h2_as_u32(pt1), 0u, b0, b1);
+  }
+  // PV per 32-dim chunk j (inside one scale group): P' = P * sv[t, group]
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int gi = (32 * j) / GROUP;
+    const __half2 b0 = __hmul2(pt0, scale_pair(t.sv[0], t.sv[1], gi));
+    const __half2 b1 = __hmul2(pt1, scale_pair(t.sv[2], t.sv[3], gi));
+    uint32_t cA[4], cB[4];
+    if (VRAW) {
+      subnormal_pairs4(t.vA[j], cA);
+      subnormal_pairs4(t.vB[j], cB);
+    } else {
+      __half2 hA[4], hB[4];
+      LanePairs<4>::centred(t.vA[j], hA);
+      LanePairs<4>::centred(t.vB[j], hB);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        cA[u] = h2_as_u32(hA[u]);
+        cB[u] = h2_as_u32(hB[u]);
+      }
+    }
+#pragma unroll
+    for (int k2 = 0; k2 < 2; ++k2)
+      mma_16816(s.acc[2 * j + k2], cA[2 * k2], cA[2 * k2 + 1], cB[2 * k2], cB[2 * k2 + 1],
+                h2_as_u32(b0), h2_as_u32(b1));
+  }
+}
+
+// VRAW: turns the uncentred accumulators into sum_t (code - 8) P' (once per warp, after the
+// stream): rows g of M-tile (j, k2) hold even code slots (scaled by 2^-24), rows g + 8 odd
+// slots (2^-20); S for (head n, group gi) lives in lane 4n + gi / 2, element gi & 1.
+template <int GROUP, bool VRAW>
+__device__ __forceinline__ void finish_stream(StreamState& s, int c) {
+  constexpr int G = 128 / GROUP;
+  if (!VRAW) return;
+#pragma unroll
+  for (int gi = 0; gi < G; ++gi) {
+    const float v = (gi & 1) ? s.vs[1] : s.vs[0];
+    const float s0 = 8.f * __shfl_sync(0xffffffffu, v, 4 * (2 * c) + (gi >> 1));
+    const float s1 = 8.f * __shfl_sync(0xffffffffu, v, 4 * (2 * c + 1) + (gi >> 1));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if ((16 * k) / GROUP != gi) continue;  // M-tile k covers dims 16k .. 16k + 15
+      s.acc[k][0] = fmaf(s.acc[k][0], 16777216.f, -s0);
+      s.acc[k][1] = fmaf(s.acc[k][1], 16777216.f, -s1);
+      s.acc[k][2] = fmaf(s.acc[k][2], 1048576.f, -s0);
+      s.acc[k][3] = fmaf(s.acc[k][3], 1048576.f, -s1);
+    }
+  }
+}
+
+// Shared-memory bytes the in-CTA merge needs (the 16 - kvh non-leading warps' states).
+__host__ __device__ constexpr size_t stream_merge_bytes(int kvh) {
+  return static_cast<size_t>(kStreamWarps - kvh) * 32 * (4 + 4 * 8) * 4;
+}
+
+// Merges the 16 / KVH consumer warps of each KV head through shared memory `buf` and writes
+// the CTA's part (m, l, acc) for query heads q0 .. q0 + nq - 1. Every thread of the CTA calls
+// it (warps >= 16 only synchronise); `buf` must no longer be written by copies in flight.
+template <int KVH>
+__device__ __forceinline__ void merge_warps_write_part(const DecodeArgs& a, float* buf, int warp,
+                                                       int lane, int q0, int nq,
+                                                       StreamState& s) {
+  constexpr int kFields = 4 + 4 * 8, WPH = kStreamWarps / KVH, D = 128;
+  const int g = lane >> 2, c = lane & 3;
+  const bool consumer = warp < kStreamWarps;
+  const int h = warp % KVH, sub = warp / KVH;
+  if (consumer && sub > 0) {
+    float* dst = buf + static_cast<size_t>((sub - 1) * KVH + h) * kFields * 32 + lane;
+    dst[0] = s.m_run[0];
+    dst[32] = s.m_run[1];
+    dst[64] = s.l_run[0];
+    dst[96] = s.l_run[1];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dst[(4 + 4 * k + e) * 32] = s.acc[k][e];
+  }
+  __syncthreads();
+  if (!consumer || sub != 0) return;
+  for (int o = 1; o < WPH; ++o) {
+    const float* src = buf + static_cast<size_t>((o - 1) * KVH + h) * kFields * 32 + lane;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const float mo = src[hh * 32], lo = src[(2 + hh) * 32];
+      const float mn = fmaxf(s.m_run[hh], mo);
+      const float a0 = mn == -INFINITY ? 0.f : fast_exp2(s.m_run[hh] - mn);
+      const float a1 = mn == -INFINITY ? 0.f : fast_exp2(mo - mn);
+      s.m_run[hh] = mn;
+      s.l_run[hh] = s.l_run[hh] * a0 + lo * a1;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        s.acc[k][hh] = s.acc[k][hh] * a0 + src[(4 + 4 * k + hh) * 32] * a1;
+        s.acc[k][2 + hh] = s.acc[k][2 + hh] * a0 + src[(4 + 4 * k + 2 + hh) * 32] * a1;
+      }
+    }
+  }
+  // This CTA's part; O^T row g of M-tile (j, k2) is dim 32j + 4g + 2k2, row g+8 the next.
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    s.l_run[0] += __shfl_xor_sync(0xffffffffu, s.l_run[0], o);
+    s.l_run[1] += __shfl_xor_sync(0xffffffffu, s.l_run[1], o);
+  }
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int n = 2 * c + hh;
+    if (n >= nq) continue;
+    const size_t row = static_cast<size_t>(blockIdx.x) * a.qh + (q0 + n);
+    if (g == 0) {
+      a.part_ml[row * 2 + 0] = s.m_run[hh];
+      a.part_ml[row * 2 + 1] = s.l_run[hh];
+    }
+    float* dst = a.part_acc + row * D + 4 * g;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2)
+        *reinterpret_cast<float2*>(dst + 32 * j + 2 * k2) =
+            make_float2(s.acc[2 * j + k2][hh], s.acc[2 * j + k2][2 + hh]);
+  }
+}
+
+}  // namespace kvb

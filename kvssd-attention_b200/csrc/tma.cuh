@@ -1,0 +1,91 @@
+// mbarrier and TMA primitives (PTX ISA: mbarrier.*, cp.async.bulk.tensor) for the TMA-fed
+// streaming kernel. No multicast form appears anywhere: every copy lands in the issuing CTA's
+// own shared memory from this GPU's memory.
+#pragma once
+
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace kvb {
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+// Makes initialised mbarriers visible to the async proxy (the TMA unit).
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Arrives and raises the phase's expected transaction count by `bytes`.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+// Non-blocking: has the phase with this parity completed?
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Potentially blocking test (the hardware may suspend the thread for a short while).
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits for the phase with this parity, giving up at `deadline_ns` (global_ns, read every 256
+// polls) or after `max_polls` polls, whichever comes first. Returns false on timeout.
+__device__ __forceinline__ bool mbar_wait_until(uint32_t bar, uint32_t parity,
+                                                unsigned long long deadline_ns,
+                                                uint32_t max_polls) {
+  for (uint32_t spin = 0;; ++spin) {
+    if (mbar_try(bar, parity)) return true;
+    if (spin >= max_polls) return false;
+    if ((spin & 255u) == 255u && global_ns() > deadline_ns) return false;
+  }
+}
+
+__device__ __forceinline__ void prefetch_tensor_map(const void* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Tiled tensor copies (no multicast) into this CTA's shared memory, completing their bytes on
+// `bar`. The innermost coordinate is always 0 here (16-byte aligned by construction).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, int x, int y,
+                                            uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, int x, int y, int z,
+                                            uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+}  // namespace kvb

@@ -22,8 +22,9 @@ ERR_DEVICE_STATUS = 5
 Q_F32, Q_F16, Q_BF16, Q_F64 = 0, 1, 2, 3
 IPC_HANDLE_BYTES = 64
 DEV_BAD_BLOCK, DEV_BAD_VALID, DEV_COMBINE_TIMEOUT, DEV_EXCHANGE_TIMEOUT = 1, 2, 4, 8
-DEV_BAD_PROBLEM = 16
+DEV_BAD_PROBLEM, DEV_STREAM_TIMEOUT = 16, 32
 PATH_AUTO, PATH_TENSOR_CORE, PATH_GENERIC, PATH_TENSOR_CORE_REGS = 0, 1, 2, 3
+PATH_TENSOR_CORE_CPASYNC = 4
 
 _c_int = ctypes.c_int
 _c_ll = ctypes.c_longlong

@@ -365,8 +365,9 @@ def read_device_status(device: torch.device | str | None = None, clear: bool = T
 
     Bit 1: a block-table entry was outside the pool; bit 2: a valid_tokens entry was outside
     [0, block_tokens] (such entries are skipped/clamped by the kernels, never dereferenced);
-    bit 4: a fused combine, bit 8: a cross-GPU exchange gave up waiting (about a second) --
-    the out/lse of that call are invalid.
+    bit 4: a fused combine, bit 8: a cross-GPU exchange, bit 32: a TMA-fed kernel's copy
+    wait gave up (about a second) -- the out/lse of that call are invalid; bit 16: a batched
+    problem descriptor was refused.
     """
     device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     stream = torch.cuda.current_stream(device)
@@ -390,6 +391,10 @@ def decode_path(head_dim: int, bits: int, group_size: int) -> int:
     return path.value
 
 
+# decode_plan kernel names of the two streaming kernels (split-KV with the fused combine)
+STREAMING_KERNELS = ("tensor_core_tma", "tensor_core_stream")
+
+
 def decode_plan(n_sel: int, block_tokens: int, query_heads: int, kv_heads: int, head_dim: int,
                 bits: int, group_size: int) -> dict:
     """Kernel choice and split count for a geometry on the current CUDA device."""
@@ -400,7 +405,8 @@ def decode_plan(n_sel: int, block_tokens: int, query_heads: int, kv_heads: int, 
             ctypes.byref(kernel), ctypes.byref(splits), ctypes.byref(parts)),
         "kvssd_b200_decode_plan",
     )
-    names = {_native.PATH_TENSOR_CORE: "tensor_core_stream",
+    names = {_native.PATH_TENSOR_CORE: "tensor_core_tma",
+             _native.PATH_TENSOR_CORE_CPASYNC: "tensor_core_stream",
              _native.PATH_TENSOR_CORE_REGS: "tensor_core_regs", _native.PATH_GENERIC: "generic"}
     return {"kernel": names[kernel.value], "path": kernel.value, "n_splits": splits.value,
             "n_parts": parts.value}

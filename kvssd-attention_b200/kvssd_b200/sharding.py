@@ -205,7 +205,7 @@ class ShardedDecoder:
                                local.group_size)
         aligned = all(t.data_ptr() % 16 == 0 for t in (local.packed_k, local.packed_v,
                                                         local.scales_k, local.scales_v))
-        ok = plan["kernel"] == "tensor_core_stream" and aligned
+        ok = plan["kernel"] in ops.STREAMING_KERNELS and aligned
         if self.transport == "peer" and not ok:
             raise RuntimeError("peer transport needs the streaming kernel's shapes and alignment")
         return ok

@@ -57,13 +57,13 @@ def path_override():
 
 
 @pytest.mark.parametrize("name", golden_names("backend_"))
-@pytest.mark.parametrize("path", [_native.PATH_AUTO, _native.PATH_TENSOR_CORE_REGS,
-                                  _native.PATH_GENERIC])
+@pytest.mark.parametrize("path", [_native.PATH_AUTO, _native.PATH_TENSOR_CORE_CPASYNC,
+                                  _native.PATH_TENSOR_CORE_REGS, _native.PATH_GENERIC])
 def test_backend_matches_reference_golden(name, path, path_override):
     g = load_npz(name)
     q, batch = golden_batch(g)
-    if path == _native.PATH_TENSOR_CORE_REGS and ops.decode_path(q.shape[1], batch.bits,
-                                                                  batch.group_size) != 1:
+    if path in (_native.PATH_TENSOR_CORE_REGS, _native.PATH_TENSOR_CORE_CPASYNC) and \
+            ops.decode_path(q.shape[1], batch.bits, batch.group_size) != 1:
         pytest.skip("shape outside the tensor-core kernels")
     path_override(path)
     out, lse = B200AttentionBackend().run(q, batch, float(g["sm_scale"]))
@@ -79,13 +79,13 @@ def test_tensor_core_path_covers_benchmark_shapes():
     for bits in (2, 4):
         assert ops.decode_path(128, bits, 32) == _native.PATH_TENSOR_CORE
     plan = ops.decode_plan(1024, 128, 32, 8, 128, 4, 32)  # the 128K-token INT4 configuration
-    assert plan["kernel"] == "tensor_core_stream", plan
+    assert plan["kernel"] == "tensor_core_tma", plan
     assert plan["n_parts"] == plan["n_splits"] <= sms
     assert ops.decode_plan(33, 128, 32, 8, 128, 2, 32)["kernel"] == "tensor_core_regs"
 
 
-@pytest.mark.parametrize("path", [_native.PATH_AUTO, _native.PATH_TENSOR_CORE_REGS,
-                                  _native.PATH_GENERIC])
+@pytest.mark.parametrize("path", [_native.PATH_AUTO, _native.PATH_TENSOR_CORE_CPASYNC,
+                                  _native.PATH_TENSOR_CORE_REGS, _native.PATH_GENERIC])
 @pytest.mark.parametrize("kvh,qh,bits", [(8, 32, 4), (8, 32, 2), (4, 16, 4), (2, 16, 4),
                                          (1, 8, 4), (8, 8, 4), (16, 32, 4)])
 def test_kernels_agree_with_oracle_across_head_layouts(kvh, qh, bits, path, path_override):
