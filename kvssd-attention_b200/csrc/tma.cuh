@@ -1,6 +1,6 @@
 // mbarrier and TMA primitives (PTX ISA: mbarrier.*, cp.async.bulk.tensor) for the TMA-fed
-// streaming kernel. No multicast form appears anywhere: every copy lands in the issuing CTA's
-// own shared memory from this GPU's memory.
+// streaming kernel. Every copy lands in the issuing CTA's own shared memory and reads this
+// GPU's own memory.
 #pragma once
 
 #include <stdint.h>
@@ -68,7 +68,7 @@ __device__ __forceinline__ void prefetch_tensor_map(const void* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
-// Tiled tensor copies (no multicast) into this CTA's shared memory, completing their bytes on
+// Tiled tensor copies into this CTA's own shared memory, completing their bytes on
 // `bar`. The innermost coordinate is always 0 here (16-byte aligned by construction).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, int x, int y,
                                             uint32_t bar, uint64_t policy) {
