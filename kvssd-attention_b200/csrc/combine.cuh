@@ -6,6 +6,8 @@
 
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace kvb {
 
 constexpr int kCombineWarps = 16;   // the caller's block is 32 * kCombineWarps threads
@@ -52,8 +54,8 @@ __device__ __forceinline__ void combine_slice_result(const float* __restrict__ p
     for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
     const float nm = fmaxf(M, cm);
     if (nm == -INFINITY) continue;  // only empty parts so far
-    const float keep = exp2f(M - nm);  // 0 while M is -inf
-    const float wp = mp == -INFINITY ? 0.f : exp2f(mp - nm);
+    const float keep = fast_exp2(M - nm);  // 0 while M is -inf
+    const float wp = mp == -INFINITY ? 0.f : fast_exp2(mp - nm);
     float ls = wp * lp;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
@@ -78,7 +80,7 @@ __device__ __forceinline__ void combine_slice_result(const float* __restrict__ p
     float ls = 0.f, t = 0.f;
 #pragma unroll
     for (int w = 0; w < kCombineWarps; ++w) {
-      const float ww = wm[w] == -INFINITY ? 0.f : exp2f(wm[w] - mx);
+      const float ww = wm[w] == -INFINITY ? 0.f : fast_exp2(wm[w] - mx);
       ls = fmaf(ww, wl[w], ls);
       t = fmaf(ww, wacc[w][lane], t);
     }
@@ -129,7 +131,7 @@ __device__ __forceinline__ void combine_slice_warp(const float* __restrict__ par
   float mx = mp;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  const float wp = (mp == -INFINITY || mx == -INFINITY) ? 0.f : exp2f(mp - mx);
+  const float wp = (mp == -INFINITY || mx == -INFINITY) ? 0.f : fast_exp2(mp - mx);
   float ls = wp * lp;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);

@@ -83,6 +83,44 @@ __device__ __forceinline__ float load_query(const void* q, int dtype, long long 
   }
 }
 
+// Eight consecutive query elements q[idx .. idx + 7] as FP32, idx a multiple of 8: vector
+// loads when the tensor is 16-byte aligned (two or four of them, all issued before use), else
+// element by element.
+__device__ __forceinline__ void load_query8(const void* q, int dtype, long long idx, float (&f)[8]) {
+  const bool vec = (reinterpret_cast<uintptr_t>(q) & 15u) == 0;
+  if (vec && (dtype == kQF16 || dtype == kQBF16)) {
+    const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(q) + idx);
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (dtype == kQF16) {
+        const __half2 h = *reinterpret_cast<const __half2*>(&u[i]);
+        f[2 * i] = __low2float(h);
+        f[2 * i + 1] = __high2float(h);
+      } else {
+        const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&u[i]);
+        f[2 * i] = __low2float(h);
+        f[2 * i + 1] = __high2float(h);
+      }
+    }
+  } else if (vec && dtype == kQF32) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(q) + idx);
+    const float4 a = p[0], b = p[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else if (vec && dtype == kQF64) {
+    const double2* p = reinterpret_cast<const double2*>(reinterpret_cast<const double*>(q) + idx);
+    const double2 a = p[0], b = p[1], c = p[2], d = p[3];
+    f[0] = static_cast<float>(a.x); f[1] = static_cast<float>(a.y);
+    f[2] = static_cast<float>(b.x); f[3] = static_cast<float>(b.y);
+    f[4] = static_cast<float>(c.x); f[5] = static_cast<float>(c.y);
+    f[6] = static_cast<float>(d.x); f[7] = static_cast<float>(d.y);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = load_query(q, dtype, idx + i);
+  }
+}
+
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t u) {
   __half2 h;
   memcpy(&h, &u, 4);

@@ -55,7 +55,8 @@ struct TmaLayout {
   static constexpr uint32_t TX = 2 * KV_BYTES + 2 * S_BYTES;
   // Scale rows use the TMA swizzle whose span equals the row (16 B rows: none).
   static constexpr uint32_t SWZ = SRB >= 128 ? 7u : SRB == 64 ? 3u : SRB == 32 ? 1u : 0u;
-  static constexpr size_t SMEM = 1024 + static_cast<size_t>(NS) * STAGE;  // + alignment slack
+  static constexpr int Q_MAX = 16384;  // query staged in shared memory up to this many bytes
+  static constexpr size_t SMEM = 1024 + static_cast<size_t>(NS) * STAGE + Q_MAX;  // + alignment
   __device__ static uint32_t swizzled(uint32_t off) { return off ^ (((off >> 7) & SWZ) << 4); }
 };
 
@@ -67,27 +68,44 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP>::THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[L::NS], empty[L::NS];
   __shared__ int stage_rows[L::NS];
+  __shared__ __align__(8) uint64_t q_bar;  // the staged query copy has landed
   const uint32_t raw_s = smem_addr(smem_raw);
   const uint32_t ring_s = (raw_s + 1023u) & ~1023u;
   uint8_t* ring = smem_raw + (ring_s - raw_s);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, c = lane & 3;
   const int h = warp % KVH, grp = warp / KVH;
-  // Programmatic stream serialization: wait for the preceding grid before the first global
-  // access, and let the next launch start early.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;");
-  const unsigned epoch =
-      a.xworld ? *reinterpret_cast<const volatile unsigned*>(a.xpeers[a.xrank]) + 1u : 0u;
-  const unsigned long long deadline = global_ns() + kCombineWaitNs;
+  // Shared-memory and parameter-space setup may overlap the preceding grid's tail.
   if (threadIdx.x == 0) {
     for (int s = 0; s < L::NS; ++s) {
       mbar_init(smem_addr(&full[s]), 1);
       mbar_init(smem_addr(&empty[s]), KVH);
     }
+    mbar_init(smem_addr(&q_bar), 1);
     mbar_init_fence();
   }
+  // Every warp of every CTA reads the whole (small) query: one bulk copy per CTA into shared
+  // memory instead of 16 warps' loads of the same lines from L2.
+  const int qsize = a.q_dtype == kQF64 ? 8 : a.q_dtype == kQF32 ? 4 : 2;
+  const uint32_t q_bytes = static_cast<uint32_t>(a.qh) * D * qsize;
+  const bool q_staged = q_bytes <= L::Q_MAX && (reinterpret_cast<uintptr_t>(a.q) & 15u) == 0;
+  uint8_t* q_smem = ring + L::NS * L::STAGE;
+  if (warp >= kStreamWarps && lane == 0) {
+    prefetch_tensor_map(&maps.k);
+    prefetch_tensor_map(&maps.v);
+    prefetch_tensor_map(&maps.ks);
+    prefetch_tensor_map(&maps.vs);
+  }
+  // Programmatic stream serialization: wait for the preceding grid before the first global
+  // access, and let the next launch start early.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
+  const unsigned long long deadline = global_ns() + kCombineWaitNs;
   __syncthreads();
+  if (q_staged && warp == kStreamWarps && lane == 0) {
+    mbar_arrive_expect_tx(smem_addr(&q_bar), q_bytes);
+    bulk_load(smem_addr(q_smem), a.q, q_bytes, smem_addr(&q_bar));
+  }
 
   const long long t_begin = a.total_tiles * blockIdx.x / a.n_splits;
   const int n_tiles = static_cast<int>(a.total_tiles * (blockIdx.x + 1) / a.n_splits - t_begin);
@@ -98,12 +116,6 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP>::THREADS, 1)
   if (warp >= kStreamWarps) {
     // ---------------- producer of group gp
     const int gp = warp - kStreamWarps;
-    if (lane == 0) {
-      prefetch_tensor_map(&maps.k);
-      prefetch_tensor_map(&maps.v);
-      prefetch_tensor_map(&maps.ks);
-      prefetch_tensor_map(&maps.vs);
-    }
     const uint64_t policy = l2_evict_first();
     BlockInfoCache cache;
 #pragma unroll 1
@@ -119,30 +131,40 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP>::THREADS, 1)
       const long long t = t_begin + k;
       const int slot = static_cast<int>(t / a.tiles_per_block);
       const int tib = static_cast<int>(t - static_cast<long long>(slot) * a.tiles_per_block);
+      const uint32_t bar = smem_addr(&full[sl]);
+      const uint32_t st = ring_s + sl * L::STAGE;
+      auto copy = [&](int blk) {
+        const int row0 = blk * a.bt + 16 * tib;
+        mbar_expect_tx(bar, L::TX);
+        tma_load_3d(st, &maps.k, 0, row0, 0, bar, policy);
+        tma_load_3d(st + L::OFF_V, &maps.v, 0, row0, 0, bar, policy);
+        tma_load_2d(st + L::OFF_KS, &maps.ks, 0, row0, bar, policy);
+        tma_load_2d(st + L::OFF_VS, &maps.vs, 0, row0, bar, policy);
+      };
+      // Without a block table the pool block is the slot itself (slot < n_sel <= n_pool), so
+      // the copies go out before the valid count is known; the arrival below then publishes
+      // the row count. With a table the entry decides whether to copy at all.
+      const bool identity = a.table == nullptr;
+      if (identity && lane == 0) copy(slot);
       int blk, valid;
       cache.lookup(a, slot, lane, blk, valid);
       const int rows = blk < 0 ? 0 : min(16, valid - 16 * tib);
       if (lane == 0) {
+        if (!identity && rows > 0) copy(blk);
         stage_rows[sl] = rows;
-        const uint32_t bar = smem_addr(&full[sl]);
-        if (rows > 0) {
-          const uint32_t st = ring_s + sl * L::STAGE;
-          const int row0 = blk * a.bt + 16 * tib;
-          mbar_arrive_expect_tx(bar, L::TX);
-          tma_load_3d(st, &maps.k, 0, row0, 0, bar, policy);
-          tma_load_3d(st + L::OFF_V, &maps.v, 0, row0, 0, bar, policy);
-          tma_load_2d(st + L::OFF_KS, &maps.ks, 0, row0, bar, policy);
-          tma_load_2d(st + L::OFF_VS, &maps.vs, 0, row0, bar, policy);
-        } else {
-          mbar_arrive(bar);  // nothing to copy: the stage is complete at once
-        }
+        mbar_arrive(bar);  // completes once the copied bytes (if any) have landed
       }
       __syncwarp();
     }
   } else {
     // ---------------- consumers
     QueryFrags<GROUP> qfr;
-    qfr.load(a, q0, nq, g, c);
+    bool q_ready = true;
+    if (q_staged)
+      q_ready = __all_sync(0xffffffffu,
+                           mbar_wait_until(smem_addr(&q_bar), 0, deadline, kTmaMaxPolls));
+    if (!q_ready && lane == 0) atomicOr(a.status, kDevStreamTimeout);
+    qfr.load(a, q_staged && q_ready ? static_cast<const void*>(q_smem) : a.q, q0, nq, g, c);
     const int ld_row = lane & 7, ld_chunk = lane >> 3;
     const uint32_t ld_off =
         static_cast<uint32_t>(ld_row * 64 + ((ld_chunk ^ ((ld_row >> 1) & 3)) << 4));
@@ -183,10 +205,12 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP>::THREADS, 1)
   }
   __syncthreads();
   if (warp >= kStreamWarps && lane == 0) {
-    // Copies still in flight can only be the group's last kTmaSlots stages (after a timeout);
-    // wait for them (bounded) before the ring is reused and the CTA exits.
+    // Copies still in flight can only be the group's last kTmaSlots stages (after a timeout)
+    // and the query copy; wait for them (bounded) before the ring is reused and the CTA exits.
     const int gp = warp - kStreamWarps;
     const unsigned long long drain_deadline = global_ns() + kCombineWaitNs;
+    if (gp == 0 && q_staged && !mbar_wait_until(smem_addr(&q_bar), 0, drain_deadline, kTmaMaxPolls))
+      atomicOr(a.status, kDevStreamTimeout);
     for (int idx = max(0, issued - kTmaSlots); idx < issued; ++idx)
       if (!mbar_wait_until(smem_addr(&full[gp * kTmaSlots + idx % kTmaSlots]),
                            (idx / kTmaSlots) & 1, drain_deadline, kTmaMaxPolls))
@@ -194,7 +218,7 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP>::THREADS, 1)
   }
   __syncthreads();
   merge_warps_write_part<KVH>(a, reinterpret_cast<float*>(ring), warp, lane, q0, nq, state);
-  if (a.fuse_combine) fused_combine_tail<D>(a, epoch, a.n_splits);
+  if (a.fuse_combine) fused_combine_tail<D>(a, a.n_splits);
 }
 
 using TmaKernel = void (*)(const DecodeArgs, const TmaMaps);

@@ -74,7 +74,7 @@ __device__ __forceinline__ void exchange_slice(const DecodeArgs& a, unsigned epo
   float num = 0.f, den = 0.f;
 #pragma unroll
   for (int r = 0; r < kMaxExchangeRanks; ++r) {
-    const float w = vl[r] == -INFINITY ? 0.f : exp2f(vl[r] - M);
+    const float w = vl[r] == -INFINITY ? 0.f : fast_exp2(vl[r] - M);
     num = fmaf(w, vo[r], num);
     den += w;
   }
@@ -86,27 +86,46 @@ __device__ __forceinline__ void exchange_slice(const DecodeArgs& a, unsigned epo
 }
 
 // Fused split-KV combine at the end of the decode grid (launched cooperatively, so all CTAs
-// are co-resident). Every CTA publishes its part and signals its arrival with one release
-// add; the n_comb highest-numbered CTAs (one per (query head, 32-dim) slice, or fewer when the
-// grid is smaller) wait until all n_splits parts have arrived and fold one or more slices
-// each. The wait is bounded: on timeout the CTA flags kDevCombineTimeout and carries on. The
-// last combiner to finish resets both counters, so the header is zero again for the next call.
+// are co-resident). Every CTA publishes its part and arrives with one acq_rel add on
+// tickets[0]; the CTA that arrives last (it sees n_splits - 1) re-arms the counter to zero,
+// publishes the exchange epoch of this call and then bumps the generation word tickets[1]
+// with a release store. The n_comb highest-numbered CTAs (one per (query head, 32-dim) slice,
+// or fewer when the grid is smaller) wait until the generation differs from the value they
+// read at their start (gen0) and fold one or more slices each; nothing is left to do after
+// the folds. The wait is bounded: on timeout the CTA flags kDevCombineTimeout, re-arms the
+// counter itself and carries on.
 template <int D>
-__device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned epoch,
-                                                   int n_parts) {
+__device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, int n_parts) {
+  // Read before this CTA's arrival (the last arriver publishes the next values): the exchange
+  // epoch of this call (completed calls + 1) and the generation word.
+  // Warp 0 (the exchange runs on it) reads the epoch, thread 0 the generation.
+  unsigned epoch = 0u, gen0 = 0u;
+  if (threadIdx.x < 32 && a.xworld)
+    epoch = *reinterpret_cast<const volatile unsigned*>(a.xpeers[a.xrank]) + 1u;
+  if (threadIdx.x == 0) gen0 = *reinterpret_cast<const volatile unsigned*>(a.tickets + 1);
   __syncthreads();  // every warp's part stores precede the CTA's release below
   constexpr int kChunks = (D + 31) / 32;
   const int n_slices = a.qh * kChunks;
   const int n_comb = min(a.n_splits, n_slices);
   const int k = static_cast<int>(blockIdx.x) - (a.n_splits - n_comb);
   if (threadIdx.x == 0) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.tickets) : "memory");
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(old) : "l"(a.tickets) : "memory");
+    if (old == static_cast<unsigned>(a.n_splits) - 1) {
+      *reinterpret_cast<volatile unsigned*>(a.tickets) = 0u;
+      // every CTA read the epoch before its arrival: publish this call's
+      if (a.xworld) *reinterpret_cast<volatile unsigned*>(a.xpeers[a.xrank]) = epoch;
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.tickets + 1), "r"(gen0 + 1u)
+                   : "memory");
+    }
     if (k >= 0) {
       const unsigned long long t0 = global_ns();
       unsigned polls = 0;
-      while (ld_acquire_gpu(a.tickets) < static_cast<unsigned>(a.n_splits)) {
+      while (ld_acquire_gpu(a.tickets + 1) == gen0) {
         if (++polls > kCombineMaxPolls || global_ns() - t0 > kCombineWaitNs) {
           atomicOr(a.status, kDevCombineTimeout);
+          atomicExch(a.tickets, 0u);  // every CTA has long arrived: re-arm for the next call
           break;
         }
         __nanosleep(32);
@@ -138,14 +157,6 @@ __device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned
       if (threadIdx.x < 32) exchange_slice<D>(a, epoch, sl, n_slices, o, l2);
     }
   }
-  }
-  if (threadIdx.x == 0) {
-    if (atomicAdd(a.tickets + 1, 1u) == static_cast<unsigned>(n_comb) - 1) {
-      atomicExch(a.tickets, 0u);
-      atomicExch(a.tickets + 1, 0u);
-      // every CTA read the epoch at its start, before its arrival: publish the completed call
-      if (a.xworld) *reinterpret_cast<volatile unsigned*>(a.xpeers[a.xrank]) = epoch;
-    }
   }
 }
 

@@ -55,25 +55,26 @@ struct QueryFrags {
   uint32_t qb[2];  // -Qg split over the four k-slices of the offset MMA (B operand)
   float unscale;   // 1 / qs
 
-  // Query heads q0 .. q0 + nq - 1 (nq <= 8) of this warp; thread (g, c) holds head g's q.
-  __device__ __forceinline__ void load(const DecodeArgs& a, int q0, int nq, int g, int c) {
-    float qv[4][2][2][2];  // [m][j2][r][dim d0 / d1], all loaded before any is used
+  // Query heads q0 .. q0 + nq - 1 (nq <= 8) of this warp from `q` (a.q, or a copy of it in
+  // shared memory); thread (g, c) holds head g's q.
+  __device__ __forceinline__ void load(const DecodeArgs& a, const void* q, int q0, int nq, int g,
+                                       int c) {
+    // Thread c needs dims 32m + 8c + 0..7 of chunk m: one 8-element load per chunk.
+    float qv[4][8];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qv[m][e] = 0.f;
+      if (g < nq) load_query8(q, a.q_dtype, static_cast<long long>(q0 + g) * D + 32 * m + 8 * c, qv[m]);
+    }
     float qmax = 0.f;
 #pragma unroll
     for (int m = 0; m < 4; ++m)
 #pragma unroll
-      for (int j2 = 0; j2 < 2; ++j2)
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const int d0 = 32 * m + 8 * c + 2 * j2 + r, d1 = d0 + 4;
-          qv[m][j2][r][0] = qv[m][j2][r][1] = 0.f;
-          if (g < nq) {
-            const long long base = static_cast<long long>(q0 + g) * D;
-            qv[m][j2][r][0] = load_query(a.q, a.q_dtype, base + d0) * a.score_scale;
-            qv[m][j2][r][1] = load_query(a.q, a.q_dtype, base + d1) * a.score_scale;
-          }
-          qmax = fmaxf(qmax, fmaxf(fabsf(qv[m][j2][r][0]), fabsf(qv[m][j2][r][1])));
-        }
+      for (int e = 0; e < 8; ++e) {
+        qv[m][e] *= a.score_scale;
+        qmax = fmaxf(qmax, fabsf(qv[m][e]));
+      }
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, o));
     const int qexp = (__float_as_uint(qmax) >> 23) & 0xff;
@@ -88,8 +89,9 @@ struct QueryFrags {
       for (int j2 = 0; j2 < 2; ++j2)
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
+          // dims d0 = 32m + 8c + 2j2 + r and d0 + 4
           const float sc = qs * (r ? 0.0625f : 1.f);
-          const __half2 hq = __floats2half2_rn(qv[m][j2][r][0] * sc, qv[m][j2][r][1] * sc);
+          const __half2 hq = __floats2half2_rn(qv[m][2 * j2 + r] * sc, qv[m][2 * j2 + r + 4] * sc);
           qf[m][j2][r] = h2_as_u32(hq);
           qsum[m] += (r ? 1152.f : 1032.f) * (__low2float(hq) + __high2float(hq));
         }

@@ -28,6 +28,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                : "memory");
 }
 
+// Raises the current phase's expected transaction count by `bytes` without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
 // Non-blocking: has the phase with this parity completed?
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   uint32_t done;
@@ -62,6 +68,16 @@ __device__ __forceinline__ bool mbar_wait_until(uint32_t bar, uint32_t parity,
     if (spin >= max_polls) return false;
     if ((spin & 255u) == 255u && global_ns() > deadline_ns) return false;
   }
+}
+
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from this GPU's
+// global memory into this CTA's shared memory, completing its bytes on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tensor_map(const void* map) {
