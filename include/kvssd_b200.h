@@ -88,10 +88,9 @@ KVSSD_B200_API int kvssd_b200_decode_workspace_size(int n_sel_blocks, int block_
  * valid_tokens entries are never dereferenced: they are skipped/clamped and recorded in the
  * workspace status word (see kvssd_b200_read_status). Outputs: out, lse as in the header.
  * The workspace (>= kvssd_b200_decode_workspace_size bytes, 16-byte aligned) starts with a
- * 2048-byte header holding that sticky status word and the fused combine's words (the
- * streaming kernel folds its split-KV parts itself; its arrival counter returns to zero at the
- * end of every call and its generation word counts calls): zero the header once after
- * allocating the workspace and leave it to the library afterwards. Calls
+ * 2048-byte header holding that sticky status word and the counters of the fused combine
+ * (the streaming kernel folds its split-KV parts itself; the counters return to zero at the
+ * end of every call): zero the header once after allocating the workspace. Calls
  * sharing one workspace must be ordered on the GPU (same stream or explicit events). */
 KVSSD_B200_API int kvssd_b200_decode(const void* query, int query_dtype, const uint8_t* packed_k,
                       const uint8_t* packed_v, const uint16_t* scales_k,

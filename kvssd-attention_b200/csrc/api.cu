@@ -56,10 +56,9 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(KVSSD_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-// Workspace header, zeroed once by the caller: the device status word (byte 0), the fused
-// combine's arrival counter and generation word (byte 128; the counter is zero again after
-// every call, the generation counts calls) and the batched decode's pair per problem (byte
-// 256, up to 148 problems).
+// Workspace header, zeroed once by the caller and zero again after every call: the device
+// status word (byte 0), the fused combine's arrival and combiner counters (byte 128) and the
+// batched decode's pair per problem (byte 256, up to 148 problems).
 constexpr size_t kHeaderBytes = 2048;
 constexpr size_t kTicketOffset = 128;
 constexpr size_t kProblemTicketOffset = 256;

@@ -100,6 +100,9 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP>::THREADS, 1)
   // access, and let the next launch start early.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
+  // Exchange epoch of this call (completed calls + 1), read before this CTA's arrival.
+  const unsigned epoch =
+      a.xworld ? *reinterpret_cast<const volatile unsigned*>(a.xpeers[a.xrank]) + 1u : 0u;
   const unsigned long long deadline = global_ns() + kCombineWaitNs;
   __syncthreads();
   if (q_staged && warp == kStreamWarps && lane == 0) {
@@ -218,7 +221,7 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP>::THREADS, 1)
   }
   __syncthreads();
   merge_warps_write_part<KVH>(a, reinterpret_cast<float*>(ring), warp, lane, q0, nq, state);
-  if (a.fuse_combine) fused_combine_tail<D>(a, a.n_splits);
+  if (a.fuse_combine) fused_combine_tail<D>(a, epoch, a.n_splits);
 }
 
 using TmaKernel = void (*)(const DecodeArgs, const TmaMaps);

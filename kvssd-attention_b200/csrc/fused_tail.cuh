@@ -86,46 +86,29 @@ __device__ __forceinline__ void exchange_slice(const DecodeArgs& a, unsigned epo
 }
 
 // Fused split-KV combine at the end of the decode grid (launched cooperatively, so all CTAs
-// are co-resident). Every CTA publishes its part and arrives with one acq_rel add on
-// tickets[0]; the CTA that arrives last (it sees n_splits - 1) re-arms the counter to zero,
-// publishes the exchange epoch of this call and then bumps the generation word tickets[1]
-// with a release store. The n_comb highest-numbered CTAs (one per (query head, 32-dim) slice,
-// or fewer when the grid is smaller) wait until the generation differs from the value they
-// read at their start (gen0) and fold one or more slices each; nothing is left to do after
-// the folds. The wait is bounded: on timeout the CTA flags kDevCombineTimeout, re-arms the
-// counter itself and carries on.
+// are co-resident). Every CTA publishes its part and signals its arrival with one release add
+// on tickets[0]; the n_comb highest-numbered CTAs (one per (query head, 32-dim) slice, or
+// fewer when the grid is smaller) wait until all n_splits parts have arrived and fold one or
+// more slices each. Each combiner counts itself on tickets[1] as soon as it has seen every
+// arrival -- the atomic's round trip overlaps its fold -- and the last one re-arms both
+// counters (zero again for the next call) and publishes the exchange epoch after its fold.
+// The wait is bounded: on timeout the CTA flags kDevCombineTimeout and carries on.
 template <int D>
-__device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, int n_parts) {
-  // Read before this CTA's arrival (the last arriver publishes the next values): the exchange
-  // epoch of this call (completed calls + 1) and the generation word.
-  // Warp 0 (the exchange runs on it) reads the epoch, thread 0 the generation.
-  unsigned epoch = 0u, gen0 = 0u;
-  if (threadIdx.x < 32 && a.xworld)
-    epoch = *reinterpret_cast<const volatile unsigned*>(a.xpeers[a.xrank]) + 1u;
-  if (threadIdx.x == 0) gen0 = *reinterpret_cast<const volatile unsigned*>(a.tickets + 1);
+__device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned epoch,
+                                                   int n_parts) {
   __syncthreads();  // every warp's part stores precede the CTA's release below
   constexpr int kChunks = (D + 31) / 32;
   const int n_slices = a.qh * kChunks;
   const int n_comb = min(a.n_splits, n_slices);
   const int k = static_cast<int>(blockIdx.x) - (a.n_splits - n_comb);
   if (threadIdx.x == 0) {
-    unsigned old;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
-                 : "=r"(old) : "l"(a.tickets) : "memory");
-    if (old == static_cast<unsigned>(a.n_splits) - 1) {
-      *reinterpret_cast<volatile unsigned*>(a.tickets) = 0u;
-      // every CTA read the epoch before its arrival: publish this call's
-      if (a.xworld) *reinterpret_cast<volatile unsigned*>(a.xpeers[a.xrank]) = epoch;
-      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.tickets + 1), "r"(gen0 + 1u)
-                   : "memory");
-    }
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.tickets) : "memory");
     if (k >= 0) {
       const unsigned long long t0 = global_ns();
       unsigned polls = 0;
-      while (ld_acquire_gpu(a.tickets + 1) == gen0) {
+      while (ld_acquire_gpu(a.tickets) < static_cast<unsigned>(a.n_splits)) {
         if (++polls > kCombineMaxPolls || global_ns() - t0 > kCombineWaitNs) {
           atomicOr(a.status, kDevCombineTimeout);
-          atomicExch(a.tickets, 0u);  // every CTA has long arrived: re-arm for the next call
           break;
         }
         __nanosleep(32);
@@ -134,6 +117,10 @@ __device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, int n_pa
   }
   if (k < 0) return;
   __syncthreads();
+  // Every combiner has passed its wait when tickets[1] reaches n_comb; the returned count is
+  // only needed after the fold.
+  unsigned combined_before = 0u;
+  if (threadIdx.x == 0) combined_before = atomicAdd(a.tickets + 1, 1u);
   if (a.xworld == 0 && n_parts <= 32) {
     // Few parts (a batched problem's handful of CTAs): one warp folds a whole slice, so the
     // CTA's 16 warps work on 16 of its slices at once.
@@ -157,6 +144,12 @@ __device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, int n_pa
       if (threadIdx.x < 32) exchange_slice<D>(a, epoch, sl, n_slices, o, l2);
     }
   }
+  }
+  if (threadIdx.x == 0 && combined_before == static_cast<unsigned>(n_comb) - 1) {
+    atomicExch(a.tickets, 0u);
+    atomicExch(a.tickets + 1, 0u);
+    // every CTA read the epoch at its start, before its arrival: publish the completed call
+    if (a.xworld) *reinterpret_cast<volatile unsigned*>(a.xpeers[a.xrank]) = epoch;
   }
 }
 

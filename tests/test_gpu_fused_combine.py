@@ -16,7 +16,7 @@ from kvssd_b200.workloads import WORKLOADS, make_layer
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
-TICKETS = 128  # byte offset of the arrival counter and generation word in the workspace header
+TICKETS = 128  # byte offset of the two combine counters in the workspace header
 
 
 @pytest.fixture(scope="module")
@@ -71,8 +71,7 @@ def test_fused_combine_equals_two_launch_combine_and_resets_counters(layer):
     ws = _workspace(w, t)
     fused = _abi_decode(w, t, ws)
     torch.cuda.synchronize()
-    words = ws[TICKETS:TICKETS + 8].view(torch.int32).tolist()
-    assert words == [0, 1], words  # arrival counter re-armed, generation advanced by one call
+    assert torch.count_nonzero(ws[TICKETS:TICKETS + 8]) == 0  # both counters re-armed
     assert _status(ws) == 0
     args = (t[0], *t[1:], w.bits, w.group_size, 1.0 / math.sqrt(w.head_dim))
     n_parts, wsp = ops.decode_split(*args)
@@ -83,7 +82,6 @@ def test_fused_combine_equals_two_launch_combine_and_resets_counters(layer):
     again = _abi_decode(w, t, ws)  # the counter was back at zero for the second call
     torch.cuda.synchronize()
     assert torch.equal(again[0], fused[0]) and torch.equal(again[1], fused[1])
-    assert ws[TICKETS:TICKETS + 8].view(torch.int32).tolist() == [0, 2]
 
 
 def test_fused_combine_wait_is_bounded_and_flagged(layer):
@@ -99,9 +97,9 @@ def test_fused_combine_wait_is_bounded_and_flagged(layer):
     elapsed = time.perf_counter() - t0
     assert _status(ws) & 4
     assert elapsed < 30
-    # the timed-out combiners re-armed the counter: the next call on the same workspace is
-    # correct without the caller touching the header
-    assert ws[TICKETS:TICKETS + 4].view(torch.int32).item() == 0
+    # the last combiner re-armed both counters after the timeout: the next call on the same
+    # workspace is correct without the caller touching them
+    assert torch.count_nonzero(ws[TICKETS:TICKETS + 8]) == 0
     ws[:4].zero_()  # the sticky status word is the caller's to clear
     out, lse = _abi_decode(w, t, ws)
     ref = ops.decode(*t, w.bits, w.group_size, 1.0 / math.sqrt(w.head_dim))
