@@ -29,7 +29,7 @@ int async_warps();
 int async_depth();
 int async_stage_bytes(int group);
 bool tma_decode_supported(int bits, int d, int group, int kvh, int bt);
-size_t tma_decode_smem(int kvh, int group);
+size_t tma_decode_smem(int kvh, int group, int bits);
 int tma_decode_threads(int kvh, int group);
 cudaError_t launch_tma_decode(const DecodeArgs& a, int n_splits, cudaStream_t s);
 using DequantKernel = void (*)(const uint8_t*, const __half*, long long, int, int, __half*,
@@ -149,12 +149,12 @@ int choose_path(int d, int bits, int group) {
 bool plan_streaming(const Geometry& g, const DeviceInfo& info, Plan& p, bool allow_tma,
                     long long pool_rows) {
   p.tma = false;
-  if (g.bits != 4 || g.d != 128 || p.n_qsub != 1 || async_warps() % g.kvh) return false;
+  if (g.d != 128 || p.n_qsub != 1 || async_warps() % g.kvh) return false;
   const size_t merge_bytes = static_cast<size_t>(async_warps() - g.kvh) * 32 * (4 + 4 * (g.d / 16)) * 4;
   const size_t max_smem = static_cast<size_t>(info.max_smem_optin) - 1024;
   if (allow_tma && g_path_override != KVSSD_B200_PATH_TENSOR_CORE_CPASYNC &&
       pool_rows < (1LL << 31) && tma_decode_supported(g.bits, g.d, g.group, g.kvh, g.bt)) {
-    const size_t smem = tma_decode_smem(g.kvh, g.group);
+    const size_t smem = tma_decode_smem(g.kvh, g.group, g.bits);
     if (smem <= max_smem && merge_bytes + 1024 <= smem) {
       p.tma = true;
       p.kernel = nullptr;

@@ -48,11 +48,13 @@ struct ScaleRow {
       memcpy(s, &w, 4);
     }
   }
-  // Scales 2i and 2i + 1 as one FP16 pair (low half = scale 2i).
+  // Scales 2i and 2i + 1 as one FP16 pair (low half = scale 2i); i may differ per thread (a
+  // select between the row's two words, never an indexed access).
   __device__ __forceinline__ uint32_t word(int i) const {
-    uint32_t w;
-    memcpy(&w, s + 2 * i, 4);
-    return w;
+    uint32_t w0, w1 = 0u;
+    memcpy(&w0, s, 4);
+    if constexpr (G == 4) memcpy(&w1, s + 2, 4);
+    return (G == 4 && i) ? w1 : w0;
   }
 };
 

@@ -41,13 +41,15 @@ struct TmaMaps {
 constexpr int kTmaSlots = 4;  // ring stages per consumer group
 constexpr uint32_t kTmaMaxPolls = 1u << 26;
 
-template <int KVH, int G>
+template <int KVH, int G, int BITS>
 struct TmaLayout {
   static constexpr int WPH = kStreamWarps / KVH;  // consumer groups = producer warps
   static constexpr int THREADS = 32 * (kStreamWarps + WPH);
   static constexpr int NS = WPH * kTmaSlots;      // ring stages
+  static constexpr int PD = 16 * BITS;            // code bytes per (token, head): 64 or 32
+  static constexpr int HEAD_TILE = 16 * PD;       // one head's 16 rows in a stage
   static constexpr int SRB = KVH * 2 * G;         // scale bytes per token row
-  static constexpr int KV_BYTES = 16 * KVH * 64;  // K (or V) bytes per stage
+  static constexpr int KV_BYTES = KVH * HEAD_TILE;  // K (or V) bytes per stage
   static constexpr int S_BYTES = 16 * SRB;        // K (or V) scale bytes per stage
   static constexpr int S_SPAN = (S_BYTES + 1023) / 1024 * 1024;
   static constexpr int OFF_V = KV_BYTES, OFF_KS = 2 * KV_BYTES, OFF_VS = OFF_KS + S_SPAN;
@@ -60,11 +62,11 @@ struct TmaLayout {
   __device__ static uint32_t swizzled(uint32_t off) { return off ^ (((off >> 7) & SWZ) << 4); }
 };
 
-template <int KVH, int GROUP>
-__global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP>::THREADS, 1)
+template <int KVH, int GROUP, int BITS>
+__global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP, BITS>::THREADS, 1)
     tma_decode_kernel(const DecodeArgs a, const __grid_constant__ TmaMaps maps) {
   constexpr int D = 128, G = D / GROUP;
-  using L = TmaLayout<KVH, G>;
+  using L = TmaLayout<KVH, G, BITS>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[L::NS], empty[L::NS];
   __shared__ int stage_rows[L::NS];
@@ -161,50 +163,82 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP>::THREADS, 1)
     }
   } else {
     // ---------------- consumers
-    QueryFrags<GROUP> qfr;
     bool q_ready = true;
     if (q_staged)
       q_ready = __all_sync(0xffffffffu,
                            mbar_wait_until(smem_addr(&q_bar), 0, deadline, kTmaMaxPolls));
     if (!q_ready && lane == 0) atomicOr(a.status, kDevStreamTimeout);
-    qfr.load(a, q_staged && q_ready ? static_cast<const void*>(q_smem) : a.q, q0, nq, g, c);
-    const int ld_row = lane & 7, ld_chunk = lane >> 3;
-    const uint32_t ld_off =
-        static_cast<uint32_t>(ld_row * 64 + ((ld_chunk ^ ((ld_row >> 1) & 3)) << 4));
+    const void* qsrc = q_staged && q_ready ? static_cast<const void*>(q_smem) : a.q;
     const uint32_t hs = static_cast<uint32_t>(h * 2 * G);  // head's byte offset in a scale row
     const uint32_t sk_off = L::swizzled(g * L::SRB + hs);
     const uint32_t sv_off = L::swizzled(2 * c * L::SRB + hs);
     const int sv_odd = static_cast<int>(L::swizzled((2 * c + 1) * L::SRB + hs)) -
                        static_cast<int>(sv_off);
     const int n_mine = grp < n_tiles ? (n_tiles - grp + L::WPH - 1) / L::WPH : 0;
-#pragma unroll 1
-    for (int i = 0; i < n_mine; ++i) {
-      const int sl = grp * kTmaSlots + i % kTmaSlots;
+    // Waits for stage i of this group; false (the warp leaves together) on timeout.
+    auto wait_stage = [&](int i, int sl) {
       const bool landed =
           mbar_wait_until(smem_addr(&full[sl]), (i / kTmaSlots) & 1, deadline, kTmaMaxPolls);
-      if (!__all_sync(0xffffffffu, landed)) {  // the warp leaves together
-        if (lane == 0) atomicOr(a.status, kDevStreamTimeout);
-        break;
-      }
-      const int rows = stage_rows[sl];
-      const uint32_t empty_bar = smem_addr(&empty[sl]);
-      if (rows <= 0) {
-        __syncwarp();
+      if (__all_sync(0xffffffffu, landed)) return true;
+      if (lane == 0) atomicOr(a.status, kDevStreamTimeout);
+      return false;
+    };
+    if constexpr (BITS == 4) {
+      QueryFrags<GROUP> qfr;
+      qfr.load(a, qsrc, q0, nq, g, c);
+      const int ld_row = lane & 7, ld_chunk = lane >> 3;
+      const uint32_t ld_off =
+          static_cast<uint32_t>(ld_row * 64 + ((ld_chunk ^ ((ld_row >> 1) & 3)) << 4));
+#pragma unroll 1
+      for (int i = 0; i < n_mine; ++i) {
+        const int sl = grp * kTmaSlots + i % kTmaSlots;
+        if (!wait_stage(i, sl)) break;
+        const int rows = stage_rows[sl];
+        const uint32_t empty_bar = smem_addr(&empty[sl]);
+        if (rows <= 0) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty_bar);
+          continue;
+        }
+        const uint32_t st = ring_s + sl * L::STAGE;
+        const uint8_t* sp = ring + sl * L::STAGE;
+        TileFrags<G> t;
+        t.template load<L::SRB>(st + h * L::HEAD_TILE, st + L::OFF_V + h * L::HEAD_TILE, ld_off,
+                                sp + L::OFF_KS + sk_off, sp + L::OFF_VS + sv_off, sv_odd);
+        float x[4];
+        qk_tile<GROUP>(t, qfr, x);
+        __syncwarp();  // every lane's loads of the stage have been consumed: release it
         if (lane == 0) mbar_arrive(empty_bar);
-        continue;
+        softmax_pv_tile<GROUP, true>(x, rows, g, qfr.unscale, t, state);
       }
-      const uint32_t st = ring_s + sl * L::STAGE;
-      const uint8_t* sp = ring + sl * L::STAGE;
-      TileFrags<G> t;
-      t.template load<L::SRB>(st + h * 1024, st + L::OFF_V + h * 1024, ld_off,
-                              sp + L::OFF_KS + sk_off, sp + L::OFF_VS + sv_off, sv_odd);
-      float x[4];
-      qk_tile<GROUP>(t, qfr, x);
-      __syncwarp();  // every lane's loads of the stage have been consumed: release it
-      if (lane == 0) mbar_arrive(empty_bar);
-      softmax_pv_tile<GROUP, true>(x, rows, g, qfr.unscale, t, state);
+      finish_stream<GROUP, true>(state, c);
+    } else {
+      QueryFrags2<GROUP> qfr;
+      qfr.load(a, qsrc, q0, nq, g, c);
+      const uint32_t ld_off = ld_off_int2(lane);
+#pragma unroll 1
+      for (int i = 0; i < n_mine; ++i) {
+        const int sl = grp * kTmaSlots + i % kTmaSlots;
+        if (!wait_stage(i, sl)) break;
+        const int rows = stage_rows[sl];
+        const uint32_t empty_bar = smem_addr(&empty[sl]);
+        if (rows <= 0) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty_bar);
+          continue;
+        }
+        const uint32_t st = ring_s + sl * L::STAGE;
+        const uint8_t* sp = ring + sl * L::STAGE;
+        TileFrags2<G> t;
+        t.template load<L::SRB>(st + h * L::HEAD_TILE, st + L::OFF_V + h * L::HEAD_TILE, ld_off,
+                                sp + L::OFF_KS + sk_off, sp + L::OFF_VS + sv_off, sv_odd);
+        float x[4];
+        qk_tile2<GROUP>(t, qfr, c, x);
+        __syncwarp();  // every lane's loads of the stage have been consumed: release it
+        if (lane == 0) mbar_arrive(empty_bar);
+        softmax_pv_tile2<GROUP>(x, rows, g, t, state);
+      }
     }
-    finish_stream<GROUP, true>(state, c);
   }
   __syncthreads();
   if (warp >= kStreamWarps && lane == 0) {
@@ -220,47 +254,54 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP>::THREADS, 1)
         atomicOr(a.status, kDevStreamTimeout);
   }
   __syncthreads();
-  merge_warps_write_part<KVH>(a, reinterpret_cast<float*>(ring), warp, lane, q0, nq, state);
+  merge_warps_write_part<KVH, BITS>(a, reinterpret_cast<float*>(ring), warp, lane, q0, nq, state);
   if (a.fuse_combine) fused_combine_tail<D>(a, epoch, a.n_splits);
 }
 
 using TmaKernel = void (*)(const DecodeArgs, const TmaMaps);
 
-template <int GROUP>
+template <int GROUP, int BITS>
 TmaKernel tma_kernel_for_heads(int kvh) {
   switch (kvh) {
-    case 4: return tma_decode_kernel<4, GROUP>;
-    case 8: return tma_decode_kernel<8, GROUP>;
-    case 16: return tma_decode_kernel<16, GROUP>;
+    case 4: return tma_decode_kernel<4, GROUP, BITS>;
+    case 8: return tma_decode_kernel<8, GROUP, BITS>;
+    case 16: return tma_decode_kernel<16, GROUP, BITS>;
+    default: return nullptr;
+  }
+}
+
+template <int BITS>
+TmaKernel tma_kernel_for_group(int group, int kvh) {
+  switch (group) {
+    case 32: return tma_kernel_for_heads<32, BITS>(kvh);
+    case 64: return tma_kernel_for_heads<64, BITS>(kvh);
     default: return nullptr;
   }
 }
 
 TmaKernel tma_kernel_for(int bits, int d, int group, int kvh) {
-  if (bits != 4 || d != 128) return nullptr;
-  switch (group) {
-    case 32: return tma_kernel_for_heads<32>(kvh);
-    case 64: return tma_kernel_for_heads<64>(kvh);
-    default: return nullptr;
-  }
+  if (d != 128) return nullptr;
+  return bits == 4 ? tma_kernel_for_group<4>(group, kvh)
+         : bits == 2 ? tma_kernel_for_group<2>(group, kvh)
+                     : nullptr;
 }
 
-template <int G>
+template <int G, int BITS>
 int tma_threads_for_heads(int kvh) {
   switch (kvh) {
-    case 4: return TmaLayout<4, G>::THREADS;
-    case 8: return TmaLayout<8, G>::THREADS;
-    case 16: return TmaLayout<16, G>::THREADS;
+    case 4: return TmaLayout<4, G, BITS>::THREADS;
+    case 8: return TmaLayout<8, G, BITS>::THREADS;
+    case 16: return TmaLayout<16, G, BITS>::THREADS;
     default: return 0;
   }
 }
 
-template <int G>
+template <int G, int BITS>
 size_t tma_smem_for_heads(int kvh) {
   switch (kvh) {
-    case 4: return TmaLayout<4, G>::SMEM;
-    case 8: return TmaLayout<8, G>::SMEM;
-    case 16: return TmaLayout<16, G>::SMEM;
+    case 4: return TmaLayout<4, G, BITS>::SMEM;
+    case 8: return TmaLayout<8, G, BITS>::SMEM;
+    case 16: return TmaLayout<16, G, BITS>::SMEM;
     default: return 0;
   }
 }
@@ -293,8 +334,10 @@ struct MapKey {
   const void* ptr;
   unsigned long long rows;
   int row_bytes;
+  int head_bytes;  // K / V: code bytes per (token, head), 64 (INT4) or 32 (INT2)
   bool operator==(const MapKey& o) const {
-    return kind == o.kind && ptr == o.ptr && rows == o.rows && row_bytes == o.row_bytes;
+    return kind == o.kind && ptr == o.ptr && rows == o.rows && row_bytes == o.row_bytes &&
+           head_bytes == o.head_bytes;
   }
 };
 
@@ -314,15 +357,18 @@ bool encode_cached(const MapKey& key, CUtensorMap* out) {
   CUtensorMap m;
   CUresult r;
   if (key.kind < 2) {
-    // K or V codes: (64 bytes, token rows, heads) with strides (heads * 64, 64); box
-    // {64, 16, heads} lands as [head][row][64 B] with the 64-byte swizzle.
-    const int heads = key.row_bytes / 64;
-    const cuuint64_t dims[3] = {64, key.rows, static_cast<cuuint64_t>(heads)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(key.row_bytes), 64};
-    const cuuint32_t box[3] = {64, 16, static_cast<cuuint32_t>(heads)};
+    // K or V codes: (pd bytes, token rows, heads) with strides (heads * pd, pd); box
+    // {pd, 16, heads} lands as [head][row][pd B] with the swizzle of the row width (64 or 32).
+    const int pd = key.head_bytes, heads = key.row_bytes / pd;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(pd), key.rows,
+                                static_cast<cuuint64_t>(heads)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(key.row_bytes),
+                                   static_cast<cuuint64_t>(pd)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(pd), 16, static_cast<cuuint32_t>(heads)};
     const cuuint32_t elem[3] = {1, 1, 1};
     r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(key.ptr), dims, strides, box,
-            elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+            elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            pd == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   } else {
     // K or V scale rows: (row bytes, token rows); box {row bytes, 16}.
@@ -355,12 +401,14 @@ bool tma_decode_supported(int bits, int d, int group, int kvh, int bt) {
          tensor_map_encoder() != nullptr;
 }
 
-size_t tma_decode_smem(int kvh, int group) {
-  return group == 32 ? tma_smem_for_heads<4>(kvh) : tma_smem_for_heads<2>(kvh);
+size_t tma_decode_smem(int kvh, int group, int bits) {
+  if (bits == 2) return group == 32 ? tma_smem_for_heads<4, 2>(kvh) : tma_smem_for_heads<2, 2>(kvh);
+  return group == 32 ? tma_smem_for_heads<4, 4>(kvh) : tma_smem_for_heads<2, 4>(kvh);
 }
 
 int tma_decode_threads(int kvh, int group) {
-  return group == 32 ? tma_threads_for_heads<4>(kvh) : tma_threads_for_heads<2>(kvh);
+  // the thread count depends on the KV heads only (16 consumers + one producer per group)
+  return group == 32 ? tma_threads_for_heads<4, 4>(kvh) : tma_threads_for_heads<2, 4>(kvh);
 }
 
 // Launches the TMA-fed decode over grid (n_splits, 1): cooperative when the fused combine is
@@ -368,7 +416,7 @@ int tma_decode_threads(int kvh, int group) {
 cudaError_t launch_tma_decode(const DecodeArgs& a, int n_splits, cudaStream_t s) {
   const TmaKernel kernel = tma_kernel_for(a.bits, a.d, a.group, a.kvh);
   if (!kernel) return cudaErrorInvalidValue;
-  const size_t smem = tma_decode_smem(a.kvh, a.group);
+  const size_t smem = tma_decode_smem(a.kvh, a.group, a.bits);
   {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -388,11 +436,12 @@ cudaError_t launch_tma_decode(const DecodeArgs& a, int n_splits, cudaStream_t s)
   }
   const unsigned long long rows = static_cast<unsigned long long>(a.n_pool) * a.bt;
   const int srb = a.kvh * 2 * (a.d / a.group);
+  const int pd = a.d * a.bits / 8;  // code bytes per (token, head)
   TmaMaps maps;
-  if (!encode_cached({0, a.kp, rows, a.kvh * 64}, &maps.k) ||
-      !encode_cached({1, a.vp, rows, a.kvh * 64}, &maps.v) ||
-      !encode_cached({2, a.ks, rows, srb}, &maps.ks) ||
-      !encode_cached({3, a.vs, rows, srb}, &maps.vs))
+  if (!encode_cached({0, a.kp, rows, a.kvh * pd, pd}, &maps.k) ||
+      !encode_cached({1, a.vp, rows, a.kvh * pd, pd}, &maps.v) ||
+      !encode_cached({2, a.ks, rows, srb, 0}, &maps.ks) ||
+      !encode_cached({3, a.vs, rows, srb, 0}, &maps.vs))
     return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(n_splits, 1, 1);

@@ -204,12 +204,13 @@ __device__ __forceinline__ void qk_tile(const TileFrags<128 / GROUP>& t, const Q
   }
 }
 
-// Online softmax of one tile's scores and the PV accumulation. rows: valid rows of the tile
-// (rows past it hold stale codes and get no weight). VRAW: subnormal V codes plus the S MMA.
-template <int GROUP, bool VRAW>
-__device__ __forceinline__ void softmax_pv_tile(float (&x)[4], int rows, int g, float unscale,
-                                                const TileFrags<128 / GROUP>& t,
-                                                StreamState& s) {
+// Online softmax of one tile's scores (rows g, g+8 x heads 2c, 2c+1; multiplied by `unscale`):
+// moves the running max lazily, rescales the state, adds the tile's probabilities to l and
+// returns them transposed for the PV B operand (pt0: tokens 2c, 2c+1 of head g; pt1: tokens
+// 2c+8, 2c+9). rows: valid rows of the tile (rows past it hold stale codes and get no weight).
+template <bool VRAW>
+__device__ __forceinline__ void softmax_tile(float (&x)[4], int rows, int g, float unscale,
+                                             StreamState& s, __half2& pt0, __half2& pt1) {
   constexpr float kLazyMax = 8.f;  // rescale only when a score beats the running max by 2^8
   if (rows < 16) {
     if (g >= rows) x[0] = x[1] = -INFINITY;
@@ -256,8 +257,17 @@ __device__ __forceinline__ void softmax_pv_tile(float (&x)[4], int rows, int g, 
   const float e2 = fast_exp2(dx[2]), e3 = fast_exp2(dx[3]);
   s.l_run[0] += e0 + e2;
   s.l_run[1] += e1 + e3;
-  const __half2 pt0 = u32_as_h2(transpose_8x8(h2_as_u32(__floats2half2_rn(e0, e1))));
-  const __half2 pt1 = u32_as_h2(transpose_8x8(h2_as_u32(__floats2half2_rn(e2, e3))));
+  pt0 = u32_as_h2(transpose_8x8(h2_as_u32(__floats2half2_rn(e0, e1))));
+  pt1 = u32_as_h2(transpose_8x8(h2_as_u32(__floats2half2_rn(e2, e3))));
+}
+
+// Softmax plus the INT4 PV step. VRAW: subnormal V codes plus the S MMA.
+template <int GROUP, bool VRAW>
+__device__ __forceinline__ void softmax_pv_tile(float (&x)[4], int rows, int g, float unscale,
+                                                const TileFrags<128 / GROUP>& t,
+                                                StreamState& s) {
+  __half2 pt0, pt1;
+  softmax_tile<VRAW>(x, rows, g, unscale, s, pt0, pt1);
   // S += P^T sv: A rows = query heads (pt0 / pt1 hold tokens 2c, 2c+1 / 2c+8, 2c+9 of head g),
   // B columns = scale groups (thread (g, c) supplies group g's scales of those tokens).
   if (VRAW) {
@@ -321,6 +331,131 @@ __device__ __forceinline__ void finish_stream(StreamState& s, int c) {
   }
 }
 
+// ---------------- INT2 (head_dim 128): 32-byte rows, 64 codes per 16-byte chunk
+//
+// A 16-byte ldmatrix row of INT2 holds 64 codes -- two scale groups of 32 -- so the INT4 trick of
+// factoring the scales out of each MMA does not apply: the tiles are dequantized in registers
+// (centred code x FP16 scale, one HMUL2 per pair: exactly kvssd's FP16 dequantized values) and
+// the MMAs run on those values. K: ldmatrix.x4 gives thread (g, c) the 16 codes of dims
+// 64ch + 16c .. +15 of rows g (matrices 0, 1: chunks ch = 0, 1) and g + 8 (matrices 2, 3); its
+// pair k (LanePairs<2>) holds dims (k, k + 8) of those 16, all in one scale group. V:
+// ldmatrix.x4.trans gives tokens (2c, 2c+1) (matrices 0, 1) and (2c+8, 2c+9) (2, 3) of dims
+// 64ch + 8g .. +7; pair k is dim 64ch + 8g + k of both tokens. PV M-tile (ch, u) takes pairs
+// 2u (rows g: dim 64ch + 8g + 2u) and 2u + 1 (rows g + 8: the next dim).
+
+// ldmatrix lane offset in a 16-row tile of 32-byte rows stored with the TMA's 32-byte swizzle
+// (16-byte chunk q of row r at q ^ ((r >> 2) & 1)): matrix m = lane / 8 covers rows
+// (m / 2) * 8 .. + 7, chunk m % 2.
+__device__ __forceinline__ uint32_t ld_off_int2(int lane) {
+  const int m = lane >> 3, row = (m >> 1) * 8 + (lane & 7), chunk = m & 1;
+  return static_cast<uint32_t>(row * 32 + ((chunk ^ ((row >> 2) & 1)) << 4));
+}
+
+// Scale gi of a scale row broadcast to both halves (gi may differ per thread).
+template <int G>
+__device__ __forceinline__ __half2 scale_bcast(const ScaleRow<G>& r, int gi) {
+  return u32_as_h2(__byte_perm(r.word(gi >> 1), 0u, (gi & 1) ? 0x3232u : 0x1010u));
+}
+
+template <int GROUP>
+struct QueryFrags2 {
+  static constexpr int D = 128;
+  // MMA t (0..3) of chunk ch: b0 = dims 64ch + 16c + {2t, 2t + 8}, b1 = {2t + 1, 2t + 9}.
+  uint32_t qf[2][4][2];
+  __device__ __forceinline__ void load(const DecodeArgs& a, const void* q, int q0, int nq, int g,
+                                       int c) {
+    float lo[2][8], hi[2][8];  // dims 64ch + 16c + 0..7 and + 8..15
+#pragma unroll
+    for (int ch = 0; ch < 2; ++ch) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) lo[ch][e] = hi[ch][e] = 0.f;
+      if (g < nq) {
+        const long long base = static_cast<long long>(q0 + g) * D + 64 * ch + 16 * c;
+        load_query8(q, a.q_dtype, base, lo[ch]);
+        load_query8(q, a.q_dtype, base + 8, hi[ch]);
+      }
+    }
+#pragma unroll
+    for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        qf[ch][t][0] = h2_as_u32(__floats2half2_rn(lo[ch][2 * t] * a.score_scale,
+                                                   hi[ch][2 * t] * a.score_scale));
+        qf[ch][t][1] = h2_as_u32(__floats2half2_rn(lo[ch][2 * t + 1] * a.score_scale,
+                                                   hi[ch][2 * t + 1] * a.score_scale));
+      }
+  }
+};
+
+template <int G>
+struct TileFrags2 {
+  uint32_t k[4], v[4];
+  ScaleRow<G> sk0, sk1, sv[4];
+  // As TileFrags::load (V and its scales first, K last), for 32-byte rows.
+  template <int SROW>
+  __device__ __forceinline__ void load(uint32_t k_tile, uint32_t v_tile, uint32_t ld_off,
+                                       const uint8_t* sk, const uint8_t* sv_row, int sv_odd) {
+    ldsm_x4_trans(v_tile + ld_off, v[0], v[1], v[2], v[3]);
+    sv[0].load(sv_row);
+    sv[1].load(sv_row + sv_odd);
+    sv[2].load(sv_row + 8 * SROW);
+    sv[3].load(sv_row + 8 * SROW + sv_odd);
+    sk0.load(sk);
+    sk1.load(sk + 8 * SROW);
+    ldsm_x4(k_tile + ld_off, k[0], k[1], k[2], k[3]);
+  }
+};
+
+// Scores of one INT2 tile (rows g, g+8 x heads 2c, 2c+1), in the log2 domain.
+template <int GROUP>
+__device__ __forceinline__ void qk_tile2(const TileFrags2<128 / GROUP>& t,
+                                         const QueryFrags2<GROUP>& q, int c, float (&x)[4]) {
+  x[0] = x[1] = x[2] = x[3] = 0.f;
+#pragma unroll
+  for (int ch = 0; ch < 2; ++ch) {
+    const int gk = (64 * ch + 16 * c) / GROUP;
+    const __half2 s0 = scale_bcast(t.sk0, gk), s1 = scale_bcast(t.sk1, gk);
+    __half2 pa[8], pb[8];
+    LanePairs<2>::centred(t.k[ch], pa);
+    LanePairs<2>::centred(t.k[2 + ch], pb);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      pa[i] = __hmul2(pa[i], s0);
+      pb[i] = __hmul2(pb[i], s1);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      mma_16816(x, h2_as_u32(pa[2 * u]), h2_as_u32(pb[2 * u]), h2_as_u32(pa[2 * u + 1]),
+                h2_as_u32(pb[2 * u + 1]), q.qf[ch][u][0], q.qf[ch][u][1]);
+  }
+}
+
+// Softmax plus the INT2 PV step (acc[4ch + u]: dims 64ch + 8g + 2u (rows g) and + 1).
+template <int GROUP>
+__device__ __forceinline__ void softmax_pv_tile2(float (&x)[4], int rows, int g,
+                                                 const TileFrags2<128 / GROUP>& t,
+                                                 StreamState& s) {
+  __half2 pt0, pt1;
+  softmax_tile<false>(x, rows, g, 1.f, s, pt0, pt1);
+#pragma unroll
+  for (int ch = 0; ch < 2; ++ch) {
+    const int gv = (64 * ch + 8 * g) / GROUP;
+    const __half2 sa = scale_pair(t.sv[0], t.sv[1], gv), sb = scale_pair(t.sv[2], t.sv[3], gv);
+    __half2 ca[8], cb[8];
+    LanePairs<2>::centred(t.v[ch], ca);
+    LanePairs<2>::centred(t.v[2 + ch], cb);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      ca[i] = __hmul2(ca[i], sa);
+      cb[i] = __hmul2(cb[i], sb);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      mma_16816(s.acc[4 * ch + u], h2_as_u32(ca[2 * u]), h2_as_u32(ca[2 * u + 1]),
+                h2_as_u32(cb[2 * u]), h2_as_u32(cb[2 * u + 1]), h2_as_u32(pt0), h2_as_u32(pt1));
+  }
+}
+
 // Shared-memory bytes the in-CTA merge needs (the 16 - kvh non-leading warps' states).
 __host__ __device__ constexpr size_t stream_merge_bytes(int kvh) {
   return static_cast<size_t>(kStreamWarps - kvh) * 32 * (4 + 4 * 8) * 4;
@@ -329,7 +464,7 @@ __host__ __device__ constexpr size_t stream_merge_bytes(int kvh) {
 // Merges the 16 / KVH consumer warps of each KV head through shared memory `buf` and writes
 // the CTA's part (m, l, acc) for query heads q0 .. q0 + nq - 1. Every thread of the CTA calls
 // it (warps >= 16 only synchronise); `buf` must no longer be written by copies in flight.
-template <int KVH>
+template <int KVH, int BITS = 4>
 __device__ __forceinline__ void merge_warps_write_part(const DecodeArgs& a, float* buf, int warp,
                                                        int lane, int q0, int nq,
                                                        StreamState& s) {
@@ -367,7 +502,8 @@ __device__ __forceinline__ void merge_warps_write_part(const DecodeArgs& a, floa
       }
     }
   }
-  // This CTA's part; O^T row g of M-tile (j, k2) is dim 32j + 4g + 2k2, row g+8 the next.
+  // This CTA's part. INT4: O^T row g of M-tile 2j + k2 is dim 32j + 4g + 2k2; INT2: row g of
+  // M-tile 4ch + u is dim 64ch + 8g + 2u; row g+8 is the next dim in both.
 #pragma unroll
   for (int o = 4; o < 32; o <<= 1) {
     s.l_run[0] += __shfl_xor_sync(0xffffffffu, s.l_run[0], o);
@@ -382,13 +518,12 @@ __device__ __forceinline__ void merge_warps_write_part(const DecodeArgs& a, floa
       a.part_ml[row * 2 + 0] = s.m_run[hh];
       a.part_ml[row * 2 + 1] = s.l_run[hh];
     }
-    float* dst = a.part_acc + row * D + 4 * g;
+    float* dst = a.part_acc + row * D + (BITS == 4 ? 4 : 8) * g;
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int k2 = 0; k2 < 2; ++k2)
-        *reinterpret_cast<float2*>(dst + 32 * j + 2 * k2) =
-            make_float2(s.acc[2 * j + k2][hh], s.acc[2 * j + k2][2 + hh]);
+    for (int k = 0; k < 8; ++k) {
+      const int off = BITS == 4 ? 32 * (k >> 1) + 2 * (k & 1) : 64 * (k >> 2) + 2 * (k & 3);
+      *reinterpret_cast<float2*>(dst + off) = make_float2(s.acc[k][hh], s.acc[k][2 + hh]);
+    }
   }
 }
 

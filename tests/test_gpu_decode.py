@@ -81,12 +81,14 @@ def test_tensor_core_path_covers_benchmark_shapes():
     plan = ops.decode_plan(1024, 128, 32, 8, 128, 4, 32)  # the 128K-token INT4 configuration
     assert plan["kernel"] == "tensor_core_tma", plan
     assert plan["n_parts"] == plan["n_splits"] <= sms
-    assert ops.decode_plan(33, 128, 32, 8, 128, 2, 32)["kernel"] == "tensor_core_regs"
+    assert ops.decode_plan(33, 128, 32, 8, 128, 2, 32)["kernel"] == "tensor_core_tma"  # INT2
+    assert ops.decode_plan(33, 128, 32, 8, 64, 4, 32)["kernel"] == "tensor_core_regs"  # D = 64
 
 
 @pytest.mark.parametrize("path", [_native.PATH_AUTO, _native.PATH_TENSOR_CORE_CPASYNC,
                                   _native.PATH_TENSOR_CORE_REGS, _native.PATH_GENERIC])
-@pytest.mark.parametrize("kvh,qh,bits", [(8, 32, 4), (8, 32, 2), (4, 16, 4), (2, 16, 4),
+@pytest.mark.parametrize("kvh,qh,bits", [(8, 32, 4), (8, 32, 2), (4, 16, 4), (4, 16, 2),
+                                         (16, 32, 2), (2, 16, 4),
                                          (1, 8, 4), (8, 8, 4), (16, 32, 4)])
 def test_kernels_agree_with_oracle_across_head_layouts(kvh, qh, bits, path, path_override):
     """Every decode kernel against the oracle for KV-head counts that change the streaming ring
@@ -297,3 +299,34 @@ def test_split_merge_property_at_c2_size():
                          layer.valid_tokens, w.bits, w.group_size, 1 / math.sqrt(w.head_dim))
     torch.cuda.synchronize()
     torch.testing.assert_close(doubled[0], 2 * whole[0], atol=1e-6, rtol=1e-5)
+
+
+@pytest.mark.parametrize("group", [32, 64])
+def test_int2_streaming_kernel_matches_oracle(group):
+    """INT2 through the TMA-fed streaming kernel (tiles dequantized in registers): both scale
+    group sizes, identity selection with ragged blocks, and a block table."""
+    pool = _pool(nb=11, bits=2, group=group, seed=group,
+                 valid=[128, 5, 128, 128, 0, 128, 77, 128, 128, 16, 128])
+    q = torch.randn(32, 128, generator=torch.Generator().manual_seed(group + 1)).half()
+    assert ops.decode_plan(11, 128, 32, 8, 128, 2, group)["kernel"] == "tensor_core_tma"
+    assert_parity(*_run(q, pool, 2, group), *_oracle(q, pool, 2, group))
+    table = [10, 0, 3, 3, 9, 6]
+    assert_parity(*_run(q, pool, 2, group, table), *_oracle(q, pool, 2, group, table))
+    assert ops.read_device_status(DEV) == 0
+
+
+def test_c3_shape_int2_outliers_recent_sink():
+    """The c3 configuration's shape at a reduced size: INT2 with 1 % outlier channels x8 and a
+    RecentSinkBlocks(1, 32) selection through a block table."""
+    import dataclasses
+
+    from kvssd_b200 import RecentSinkBlocks
+    from kvssd_b200.workloads import WORKLOADS, make_layer
+
+    w = dataclasses.replace(WORKLOADS["c3"], tokens=64 * 128, seed=33)
+    layer = make_layer(w, 0, "cpu")
+    sel = RecentSinkBlocks(w.sink, w.recent).select(list(range(layer.packed_k.shape[0])))
+    pool = (layer.packed_k, layer.packed_v, layer.scales_k, layer.scales_v, layer.valid_tokens)
+    out, lse = _run(layer.query, pool, 2, 32, sel)
+    assert_parity(out, lse, *_oracle(layer.query, pool, 2, 32, sel))
+    assert ops.read_device_status(DEV) == 0
