@@ -57,7 +57,7 @@ enum kvssd_b200_path {
   KVSSD_B200_PATH_AUTO = 0,
   KVSSD_B200_PATH_TENSOR_CORE = 1,     /* mma.sync split-KV tile math (head_dim 64/128/256,
                                           group >= 16); streamed where it qualifies: TMA-fed
-                                          (INT4, head_dim 128, 4/8/16 KV heads), else
+                                          (INT4/INT2, head_dim 128, 4/8/16 KV heads), else
                                           cp.async-fed */
   KVSSD_B200_PATH_GENERIC = 2,         /* CUDA-core split-KV kernel (any head_dim <= 256) */
   KVSSD_B200_PATH_TENSOR_CORE_REGS = 3, /* override only: tensor-core tile math fed by
@@ -260,7 +260,7 @@ KVSSD_B200_API int kvssd_b200_ipc_close(void* buffer);
  * buffer's header), so they may be captured in a CUDA graph. A rank that does not arrive
  * within about a second makes the others flag status bit 8 (kvssd_b200_read_status) and
  * return; the ranks' call numbers then differ, and the group re-zeroes its buffers (after a
- * barrier) before the next call. Requires the streaming kernel's shapes (INT4, head_dim 128,
+ * barrier) before the next call. Requires a streaming kernel's shapes (INT4 or INT2, head_dim 128,
  * group 32/64, 16-byte aligned operands) and a cooperative launch; other arguments as
  * kvssd_b200_decode. No reference counterpart. */
 KVSSD_B200_API int kvssd_b200_decode_exchange(const void* query, int query_dtype,

@@ -673,8 +673,8 @@ int kvssd_b200_decode_exchange(const void* query, int query_dtype, const uint8_t
   if (st) return st;
   if (!p.streaming)
     return fail(KVSSD_B200_ERR_UNSUPPORTED,
-                "the fused exchange needs the streaming kernel (INT4, head_dim 128, group 32/64, "
-                "16-byte aligned operands)");
+                "the fused exchange needs a streaming kernel (INT4 or INT2 with 4/8/16 KV heads, "
+                "head_dim 128, group 32/64, 16-byte aligned operands)");
   a.xworld = world;
   a.xrank = rank;
   for (int r = 0; r < world; ++r) a.xpeers[r] = static_cast<uint8_t*>(buffers[r]);

@@ -192,7 +192,7 @@ class ShardedDecoder:
         self._peer_out: tuple[torch.Tensor, torch.Tensor] | None = None
 
     def _use_peer(self, query: torch.Tensor, local: PackedBatch) -> bool:
-        """Token shards on CUDA with the native streaming kernel (INT4, head_dim 128, group
+        """Token shards on CUDA with a native streaming kernel (INT4 or INT2, head_dim 128, group
         32/64, 16-byte aligned operands) and more than one rank: one fused kernel per rank."""
         if self.transport == "nccl" or self.mode != "tokens" or self.decode_fn is not None:
             return False
