@@ -214,6 +214,14 @@ int make_plan(const Geometry& g, bool aligned, bool allow_stream, Plan& p,
             : static_cast<long long>(info.sms) * occupancy(p.kernel, p.threads) / p.n_head_groups;
   const long long by_work = (p.total_tiles + 2 * p.wph - 1) / (2 * p.wph);
   long long splits = std::max(1LL, std::min(resident, by_work));
+  if (p.streaming && splits > 32) {
+    // The fused combine folds one (query head, 32-dim) slice per combining CTA with all of the
+    // CTA's warps (above 32 parts); with fewer CTAs than slices a CTA folds several in turn,
+    // ~2.5 us each. So the grid gets at least one CTA per slice where the SMs allow it (CTAs
+    // past the work write empty parts).
+    const long long n_slices = static_cast<long long>(g.qh) * ((g.d + 31) / 32);
+    splits = std::min(resident, std::max(splits, n_slices));
+  }
   const int parts_per_split = p.streaming ? 1 : p.wph;  // merged in-CTA by the streaming kernel
   splits = std::min<long long>(splits, kMaxParts / parts_per_split);
   p.n_splits = static_cast<int>(splits);

@@ -330,3 +330,24 @@ def test_c3_shape_int2_outliers_recent_sink():
     out, lse = _run(layer.query, pool, 2, 32, sel)
     assert_parity(out, lse, *_oracle(layer.query, pool, 2, 32, sel))
     assert ops.read_device_status(DEV) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32, torch.float64])
+def test_unaligned_query_takes_the_element_load_path(dtype):
+    """A query view that is not 16-byte aligned (offset by one element) is read element by
+    element instead of through the per-CTA bulk copy / vector loads; results are identical to
+    the aligned query's."""
+    pool = _pool(nb=6, seed=5, valid=[128, 128, 90, 128, 1, 128])
+    q = torch.randn(32, 128, generator=torch.Generator().manual_seed(6)).to(dtype)
+    backing = torch.empty(32 * 128 + 1, dtype=dtype, device=DEV)
+    unaligned = backing[1:].view(32, 128)
+    unaligned.copy_(q.to(DEV))
+    assert unaligned.data_ptr() % 16 != 0
+    dev = [t.to(DEV) for t in pool]
+    scale = 1.0 / math.sqrt(128)
+    out_u, lse_u = ops.decode(unaligned, *dev, 4, 32, scale)
+    out_a, lse_a = ops.decode(q.to(DEV).contiguous(), *dev, 4, 32, scale)
+    torch.cuda.synchronize()
+    assert torch.equal(out_u, out_a) and torch.equal(lse_u, lse_a)
+    assert_parity(out_u, lse_u, *_oracle(q.float(), pool, 4, 32))
+    assert ops.read_device_status(DEV) == 0
