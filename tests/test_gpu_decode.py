@@ -1,5 +1,5 @@
 """GPU parity of the fused decode kernels against the reference's golden outputs and the CPU
-oracle. Tolerance: outputs cast to FP16 within max-abs 2e-3 and
+oracle. Tolerance (the parity target of this path): outputs cast to FP16 within max-abs 2e-3 and
 rel 1e-2 of the reference CPU decode; LSE within 5e-3 abs + 1e-3 rel. Unpacked codes and FP16
 dequantized values are bit-exact."""
 
