@@ -351,3 +351,18 @@ def test_unaligned_query_takes_the_element_load_path(dtype):
     assert torch.equal(out_u, out_a) and torch.equal(lse_u, lse_a)
     assert_parity(out_u, lse_u, *_oracle(q.float(), pool, 4, 32))
     assert ops.read_device_status(DEV) == 0
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+@pytest.mark.parametrize("kvh,qh", [(4, 16), (16, 32)])
+def test_streaming_group64_scale_row_layouts(kvh, qh, bits):
+    """Group 64 with 4 and 16 KV heads: the streaming kernel's scale rows are then 16 and 64
+    bytes (no swizzle / the 64-byte swizzle) -- layouts the group-32 cases do not reach."""
+    pool = _pool(nb=7, kvh=kvh, bits=bits, group=64, seed=kvh + bits,
+                 valid=[128, 128, 33, 128, 0, 128, 9])
+    q = torch.randn(qh, 128, generator=torch.Generator().manual_seed(kvh * 7 + bits)).half()
+    assert ops.decode_plan(7, 128, qh, kvh, 128, bits, 64)["kernel"] == "tensor_core_tma"
+    assert_parity(*_run(q, pool, bits, 64), *_oracle(q, pool, bits, 64))
+    table = [6, 1, 1, 3, 0]
+    assert_parity(*_run(q, pool, bits, 64, table), *_oracle(q, pool, bits, 64, table))
+    assert ops.read_device_status(DEV) == 0
