@@ -164,6 +164,16 @@ def cpu_oracle_run(seconds: float, blocks: int | None = None, min_runs: int = 1)
                       f"{cpu_threads()} host threads merged exactly"}
 
 
+def workload_text(world: int) -> str:
+    """The workload both arms report (the reference arm measures a bounded sample of it)."""
+    return (f"{WORKLOAD}: 1 layer x 131072 tokens per GPU, INT4 group 32 FP16 scales, 8 KV heads "
+            "x 128, 32 query heads (GQA 4), block 128, AllBlocks"
+            + (f"; {world} GPUs split one {world * 131072}-token context by token-block ranges; "
+               "each rank's decode kernel pushes its combined slices to every rank over NVLink "
+               "peer stores and merges them exactly (one kernel per rank per step)"
+               if world > 1 else ""))
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -191,7 +201,8 @@ def run_reference(args) -> None:
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{WORKLOAD} shape, {blocks}-block sample per step",
+        "config": {"workload": workload_text(1),
+                   "sample": f"{blocks} of the 1024 blocks per step, timed on the host cores",
                    "kv_heads": w.kv_heads, "head_dim": w.head_dim, "query_heads": w.query_heads,
                    "block_tokens": w.block_tokens, "bits": w.bits, "group_size": w.group_size},
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cpu_threads(), "kind": "port",
@@ -571,12 +582,7 @@ def run_ours(args) -> None:
         "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
         "config": {
-            "workload": (f"{WORKLOAD}: 1 layer x 131072 tokens per GPU, INT4 group 32 FP16 "
-                         "scales, 8 KV heads x 128, 32 query heads (GQA 4), block 128, AllBlocks"
-                         + (f"; {world} GPUs split one {world * 131072}-token context by "
-                            "token-block ranges; each rank's decode kernel pushes its combined "
-                            "slices to every rank over NVLink peer stores and merges them exactly "
-                            "(one kernel per rank per step)" if world > 1 else "")),
+            "workload": workload_text(world),
             "us_per_layer_decode": ms * 1e3,
             "packed_kv_bytes_per_gpu": nbytes,
             "hbm_peak_gbs": peak,
