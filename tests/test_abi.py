@@ -83,7 +83,13 @@ def test_path_selection_table():
     assert p.value == 2
     assert lib.kvssd_b200_set_path_override(1) == 0
     assert lib.kvssd_b200_decode_path(32, 4, 16, ctypes.byref(p)) == _native.ERR_UNSUPPORTED
+    # the cp.async-fed streaming kernel is a member of the tensor-core family: same answers
+    assert lib.kvssd_b200_set_path_override(_native.PATH_TENSOR_CORE_CPASYNC) == 0
+    assert lib.kvssd_b200_decode_path(128, 4, 32, ctypes.byref(p)) == 0
+    assert p.value == _native.PATH_TENSOR_CORE
+    assert lib.kvssd_b200_decode_path(32, 4, 16, ctypes.byref(p)) == _native.ERR_UNSUPPORTED
     assert lib.kvssd_b200_set_path_override(0) == 0
+    assert lib.kvssd_b200_set_path_override(5) == _native.ERR_INVALID_ARGUMENT
     assert lib.kvssd_b200_set_path_override(7) == _native.ERR_INVALID_ARGUMENT
 
 
