@@ -30,7 +30,6 @@ import subprocess
 import sys
 import tempfile
 import time
-from dataclasses import replace
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
@@ -67,6 +66,7 @@ def parse_args():
                          "e2e leg or CPU baseline)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target duration of the CPU-baseline sample")
+    ap.add_argument("--no-c4", action="store_true", help="skip the c4 multi-layer leg")
     return ap.parse_args()
 
 
@@ -133,39 +133,38 @@ def cpu_threads() -> int:
     return os.cpu_count() or 1
 
 
-def sample_blocks() -> int:
-    """Blocks per CPU sample: 8-block chunks, several per host thread, at most a full layer."""
-    return min(1024, max(64, 8 * cpu_threads()))
-
-
-def cpu_oracle_run(seconds: float, blocks: int | None = None, min_runs: int = 1) -> dict:
-    """Times the oracle (numpy restatement of kvssd's reference backend) on a bounded sample
-    of the benchmark workload with the same shapes and distributions."""
+def cpu_layer():
+    """The benchmark layer (all 1024 blocks of the c2 workload) as numpy arrays for the oracle."""
     from kvssd_b200.workloads import WORKLOADS, make_layer
+
+    w = WORKLOADS[WORKLOAD]
+    layer = make_layer(w, 0, "cpu")
+    arrays = [t.numpy() for t in (layer.packed_k, layer.packed_v, layer.scales_k,
+                                  layer.scales_v, layer.valid_tokens)]
+    return w, layer.query.float().numpy(), arrays
+
+
+def cpu_oracle_run(seconds: float, min_runs: int = 1) -> dict:
+    """Times the oracle (numpy restatement of kvssd's reference backend) on the benchmark's own
+    workload -- one whole c2 layer per run -- repeated for about ``seconds``."""
     from oracle import kvssd_oracle as orc
 
-    blocks = blocks or sample_blocks()
-    w = replace(WORKLOADS[WORKLOAD], tokens=blocks * WORKLOADS[WORKLOAD].block_tokens)
-    layer = make_layer(w, 0, "cpu")
-    args = [t.numpy() for t in (layer.packed_k, layer.packed_v, layer.scales_k, layer.scales_v,
-                                layer.valid_tokens)]
-    q = layer.query.float().numpy()
-    nbytes = blocks * w.bytes_per_block
+    w, q, arrays = cpu_layer()
+    nbytes = w.blocks_per_layer * w.bytes_per_block
     runs, t0 = 0, time.perf_counter()
     while runs < min_runs or time.perf_counter() - t0 < seconds:
-        orc.decode(q, *args, w.bits, w.group_size, 1 / math.sqrt(w.head_dim))
+        orc.decode(q, *arrays, w.bits, w.group_size, 1 / math.sqrt(w.head_dim))
         runs += 1
     dt = time.perf_counter() - t0
     return {"value": nbytes * runs / dt / 1e9, "unit": "GB/s", "cores": cpu_threads(),
-            "kind": "port", "seconds": dt, "runs": runs,
-            "sample": f"{blocks} of 1024 blocks ({blocks * w.block_tokens} tokens) of the c2 "
-                      f"workload shape per run, {runs} runs; numpy restatement of "
-                      "src/kvssd/backends/reference.py, 8-block chunks on "
-                      f"{cpu_threads()} host threads merged exactly"}
+            "kind": "port", "seconds": dt, "runs": runs, "sample_blocks": w.blocks_per_layer,
+            "sample": f"the whole c2 layer ({w.blocks_per_layer} blocks, {w.tokens} tokens) per "
+                      f"run, {runs} runs; numpy restatement of src/kvssd/backends/reference.py, "
+                      f"8-block chunks on {cpu_threads()} host threads merged exactly"}
 
 
 def workload_text(world: int) -> str:
-    """The workload both arms report (the reference arm measures a bounded sample of it)."""
+    """The workload both arms report."""
     return (f"{WORKLOAD}: 1 layer x 131072 tokens per GPU, INT4 group 32 FP16 scales, 8 KV heads "
             "x 128, 32 query heads (GQA 4), block 128, AllBlocks"
             + (f"; {world} GPUs split one {world * 131072}-token context by token-block ranges; "
@@ -175,26 +174,22 @@ def workload_text(world: int) -> str:
 
 
 def run_reference(args) -> None:
+    """The reference arm: kvssd's reference backend algorithm (the oracle port) on the host
+    cores, on the same workload as the measured arm (the whole c2 layer per step)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from kvssd_b200.workloads import WORKLOADS, make_layer
     from oracle import kvssd_oracle as orc
 
-    blocks = sample_blocks()
-    w = replace(WORKLOADS[WORKLOAD], tokens=blocks * WORKLOADS[WORKLOAD].block_tokens)
-    layer = make_layer(w, 0, "cpu")
-    tensors = [t.numpy() for t in (layer.packed_k, layer.packed_v, layer.scales_k,
-                                   layer.scales_v, layer.valid_tokens)]
-    q = layer.query.float().numpy()
-    step = lambda: orc.decode(q, *tensors, w.bits, w.group_size, 1 / math.sqrt(w.head_dim))  # noqa: E731
+    w, q, arrays = cpu_layer()
+    step = lambda: orc.decode(q, *arrays, w.bits, w.group_size, 1 / math.sqrt(w.head_dim))  # noqa: E731
     for _ in range(max(args.warmup, 0)):
         step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step()
     dt = (time.perf_counter() - t0) / args.steps
-    nbytes = blocks * w.bytes_per_block
+    nbytes = w.blocks_per_layer * w.bytes_per_block
     value = nbytes / dt / 1e9
     emit({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
@@ -202,12 +197,15 @@ def run_reference(args) -> None:
         "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": workload_text(1),
-                   "sample": f"{blocks} of the 1024 blocks per step, timed on the host cores",
+                   "sample": f"the whole layer ({w.blocks_per_layer} blocks) per step, timed on "
+                             "the host cores (rank 0 only when launched on several GPUs)",
+                   "sample_blocks": w.blocks_per_layer,
                    "kv_heads": w.kv_heads, "head_dim": w.head_dim, "query_heads": w.query_heads,
                    "block_tokens": w.block_tokens, "bits": w.bits, "group_size": w.group_size},
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cpu_threads(), "kind": "port",
-                         "sample": f"{blocks} blocks ({blocks * w.block_tokens} tokens) of the c2 "
-                                   "shape per step; numpy restatement of kvssd's reference "
+                         "sample_blocks": w.blocks_per_layer,
+                         "sample": f"the whole c2 layer ({w.blocks_per_layer} blocks, {w.tokens} "
+                                   "tokens) per step; numpy restatement of kvssd's reference "
                                    "backend, 8-block chunks on all host threads merged exactly "
                                    "(the reference is Python and is not installed on the GPU "
                                    "host)"},
@@ -272,26 +270,29 @@ def pipeline_legs(w, base, q, scale, device, rank, args) -> dict:
         "record_decode_on_gpu": {
             "value": record_bytes / (rec_ms * 1e-3) / 1e9, "unit": "GB/s of records",
             "us_per_layer": rec_ms * 1e3,
-            "note": "1024 raw records resident in HBM -> PackedBatch + CRC-32 check"},
+            "hbm_bytes_per_layer": record_bytes + nbytes,
+            "hbm_frac": (record_bytes + nbytes) / (rec_ms * 1e-3) / 1e9 / peaks()[0],
+            "note": "1024 raw records resident in HBM -> PackedBatch + CRC-32 check (reads the "
+                    "records, writes the packed KV: hbm_frac counts both)"},
     }
 
 
-def graph_time(fn, device, reps: int = 20) -> float:
-    """Device ms per call of ``fn``: ``reps`` calls captured in one CUDA graph (after 3 eager
+def graph_time(fn, device, reps: int = 20, rotate: int = 1) -> float:
+    """Device ms per call of ``fn(i)``: ``reps`` calls captured in one CUDA graph (after 3 eager
     warm-up calls and one on the capture stream), one warm replay, then one timed replay."""
     stream = torch.cuda.current_stream(device)
-    for _ in range(3):
-        fn()
+    for i in range(3):
+        fn(i)
     side = torch.cuda.Stream(device)
     side.wait_stream(stream)
     with torch.cuda.stream(side):
-        fn()
+        fn(0)
     stream.wait_stream(side)
     torch.cuda.synchronize(device)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=side):
-        for _ in range(reps):
-            fn()
+        for i in range(reps):
+            fn(i)
     g.replay()
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -303,66 +304,124 @@ def graph_time(fn, device, reps: int = 20) -> float:
     return e0.elapsed_time(e1) / reps
 
 
-def c4_legs(w, base, device, args) -> dict:
-    """The multi-layer step of c4 on one GPU: 32 layers x 65536 tokens (each layer 512 blocks of
-    distinct memory: halves of 16 copies of this workload's pool), each with its own query,
-    decoded by one batched launch and by 32 single decodes; CUDA-graph replays, device time."""
+def c4_step(w, base, device, rank: int, world: int, dist):
+    """The c4 multi-layer step, KV-head sharded over ``world`` ranks: 32 layers x 65536 tokens
+    (each layer 512 blocks of distinct memory, halves of 16 copies of this rank's c2 pool), each
+    with its own query. Rank r owns KV heads [r*8/N, (r+1)*8/N) of every layer and their query
+    heads (kvssd's GQA map), re-laid head-contiguous; a step is one batched launch over its 32
+    layers plus, for N > 1, one NCCL all-gather of the output rows of all layers."""
     from kvssd_b200 import ops
+    from kvssd_b200.sharding import head_shard
 
     layers, per = 32, w.blocks_per_layer // 2
-    copies = [[t.clone() for t in (base.packed_k, base.packed_v, base.scales_k, base.scales_v,
-                                   base.valid_tokens)] for _ in range(layers // 2)]
+    kv_lo, kv_hi, q_lo, q_hi = head_shard(w.kv_heads, w.query_heads, rank, world)
+    cut = lambda t: t[:, :, kv_lo:kv_hi].contiguous()  # noqa: E731
+    copies = [[cut(t) for t in (base.packed_k, base.packed_v, base.scales_k, base.scales_v)]
+              + [base.valid_tokens.clone()] for _ in range(layers // 2)]
     pools = [[t[h * per:(h + 1) * per] for t in copies[i // 2]] for i, h in
              ((i, i % 2) for i in range(layers))]
     gen = torch.Generator().manual_seed(4)
-    queries = [torch.randn(w.query_heads, w.head_dim, generator=gen).half().to(device)
-               for _ in range(layers)]
-    problems = [(q, *p, None) for q, p in zip(queries, pools)]
-    scale = 1 / math.sqrt(w.head_dim)
-    batch = ops.BatchedDecode(problems, w.bits, w.group_size, scale)
-    batched_ms = graph_time(batch.run, device)
-    single_ms = graph_time(lambda: [ops.decode(q, *p, w.bits, w.group_size, scale)
-                                    for q, p in zip(queries, pools)], device)
-    step_bytes = layers * per * w.bytes_per_block
-    return {
-        "workload": "c4 on 1 GPU: 32 layers x 65536 tokens, INT4 g32, 8 KV heads, GQA 4",
-        "batched_one_launch": {"us_per_layer": batched_ms * 1e3 / layers,
-                               "GB/s": step_bytes / (batched_ms * 1e-3) / 1e9},
-        "one_decode_per_layer": {"us_per_layer": single_ms * 1e3 / layers,
-                                 "GB/s": step_bytes / (single_ms * 1e-3) / 1e9},
-        "bytes_per_step": step_bytes,
-    }
+    queries = [torch.randn(w.query_heads, w.head_dim, generator=gen).half()[q_lo:q_hi]
+               .contiguous().to(device) for _ in range(layers)]
+    rows = q_hi - q_lo
+    out = torch.empty((layers, rows, w.head_dim), dtype=torch.float32, device=device)
+    lse = torch.empty((layers, rows), dtype=torch.float32, device=device)
+    batch = ops.BatchedDecode([(q, *p, None) for q, p in zip(queries, pools)], w.bits,
+                              w.group_size, 1 / math.sqrt(w.head_dim), out=out, lse=lse)
+    gathered = None
+    if world > 1:
+        gathered = torch.empty((world, layers, rows, w.head_dim), dtype=torch.float32,
+                               device=device)
+
+    def step(i: int):
+        batch.run()
+        if gathered is not None:
+            dist.all_gather_into_tensor(gathered.view(-1), out.view(-1))
+
+    return step, batch, layers * per * w.bytes_per_block * (kv_hi - kv_lo) // w.kv_heads
 
 
 def small_config_legs(device) -> dict:
-    """Latency of the other single-GPU configurations (device time per decode, CUDA-graph
-    replays): c1 (8192 tokens, INT4, all 64 blocks) and c3 (INT2 with 1 % outlier channels x8,
-    RecentSinkBlocks(1, 32) over 1024 blocks: 33 blocks through a block table)."""
+    """Latency of the other single-GPU configurations, CUDA-graph replays, device time per
+    decode, both with the inputs L2-warm and cold: c1 (8192 tokens, INT4, all 64 blocks) and
+    c3 (INT2 with 1 % outlier channels x8, RecentSinkBlocks(1, 32) over 1024 blocks: 33 blocks
+    through a block table). Cold: the selected blocks are replicated into R distinct copies
+    (R x selected bytes > 126 MB L2) and step i reads copy i % R (c1: the pool view of copy r;
+    c3: one pool of R x 33 blocks with one block table per copy, the RecentSink order kept)."""
     from kvssd_b200 import RecentSinkBlocks, ops
     from kvssd_b200.workloads import WORKLOADS, make_layer
 
     res = {}
     for name in ("c1", "c3"):
         w = WORKLOADS[name]
-        lay = make_layer(w, 0, "cpu")
-        t = [x.to(device) for x in (lay.query, lay.packed_k, lay.packed_v, lay.scales_k,
-                                    lay.scales_v, lay.valid_tokens)]
+        lay = make_layer(w, 0, device)
+        q = lay.query
+        pool = [lay.packed_k, lay.packed_v, lay.scales_k, lay.scales_v, lay.valid_tokens]
         sel = list(range(lay.packed_k.shape[0]))
         table = None
         if w.sink is not None:
             sel = RecentSinkBlocks(w.sink, w.recent).select(sel)
             table = torch.tensor(sel, dtype=torch.int32, device=device)
         scale = 1 / math.sqrt(w.head_dim)
-        us = graph_time(lambda: ops.decode(*t, w.bits, w.group_size, scale, block_table=table),
-                        device, reps=50) * 1e3
+        warm_us = graph_time(lambda i: ops.decode(q, *pool, w.bits, w.group_size, scale,
+                                                  block_table=table), device, reps=50) * 1e3
         nbytes = len(sel) * w.bytes_per_block
-        plan = ops.decode_plan(len(sel), w.block_tokens, w.query_heads, w.kv_heads, w.head_dim,
+        reps = -(-int(1.2 * 126e6) // nbytes)  # copies whose bytes exceed L2 by 20 %
+        idx = torch.tensor(sel, device=device, dtype=torch.long)
+        picked = [t.index_select(0, idx) for t in pool]
+        big = [t.repeat(reps, *([1] * (t.ndim - 1))) for t in picked]
+        n_sel = len(sel)
+        if table is None:
+            views = [[t[r * n_sel:(r + 1) * n_sel] for t in big] for r in range(reps)]
+            cold = lambda i: ops.decode(q, *views[i % reps], w.bits, w.group_size, scale)  # noqa: E731
+        else:
+            tables = [torch.arange(r * n_sel, (r + 1) * n_sel, dtype=torch.int32, device=device)
+                      for r in range(reps)]
+            cold = lambda i: ops.decode(q, *big, w.bits, w.group_size, scale,  # noqa: E731
+                                        block_table=tables[i % reps])
+        cold_us = graph_time(cold, device, reps=max(50, 2 * reps)) * 1e3
+        plan = ops.decode_plan(n_sel, w.block_tokens, w.query_heads, w.kv_heads, w.head_dim,
                                w.bits, w.group_size)
-        res[name] = {"us_per_decode": us, "GB/s": nbytes / (us * 1e-6) / 1e9,
-                     "inputs": "resident, L2-warm between replays (a latency figure)",
-                     "selected_blocks": len(sel), "packed_kv_bytes": nbytes,
-                     "kernel": plan["kernel"]}
+        res[name] = {"us_per_decode": cold_us, "GB/s": nbytes / (cold_us * 1e-6) / 1e9,
+                     "us_per_decode_l2_warm": warm_us,
+                     "GB/s_l2_warm": nbytes / (warm_us * 1e-6) / 1e9,
+                     "inputs": f"cold: {reps} copies of the selected blocks "
+                               f"({reps * nbytes / 1e6:.0f} MB > 126 MB L2) rotated step by "
+                               "step; warm: the same blocks every step",
+                     "selected_blocks": n_sel, "packed_kv_bytes": nbytes,
+                     "kernel": plan["kernel"], "ctas": plan["n_splits"]}
+        del big, picked
     return res
+
+
+def int2_leg(device, copies: int = 3) -> dict:
+    """INT2 over the whole c3 cache (131072 tokens, 1 % outlier channels x8, AllBlocks),
+    inputs rotated over ``copies`` copies (> L2), CUDA-graph replays."""
+    from kvssd_b200 import ops
+    from kvssd_b200.workloads import WORKLOADS, make_layer
+
+    w = WORKLOADS["c3"]
+    lay = make_layer(w, 0, device)
+    pools = [[lay.packed_k, lay.packed_v, lay.scales_k, lay.scales_v, lay.valid_tokens]]
+    for _ in range(1, copies):
+        pools.append([t.clone() for t in pools[0]])
+    scale = 1 / math.sqrt(w.head_dim)
+    us = graph_time(lambda i: ops.decode(lay.query, *pools[i % copies], w.bits, w.group_size,
+                                         scale), device, reps=30) * 1e3
+    nbytes = w.blocks_per_layer * w.bytes_per_block
+    plan = ops.decode_plan(w.blocks_per_layer, w.block_tokens, w.query_heads, w.kv_heads,
+                           w.head_dim, w.bits, w.group_size)
+    peak = peaks()[0]
+    return {"workload": "INT2 g32, 131072 tokens (1024 blocks), 8 KV heads x 128, 32 query "
+                        "heads, 1 % outlier channels x8, AllBlocks",
+            "us_per_decode": us, "GB/s": nbytes / (us * 1e-6) / 1e9,
+            "frac": nbytes / (us * 1e-6) / 1e9 / peak, "packed_kv_bytes": nbytes,
+            "l2": f"inputs rotated over {copies} copies ({copies * nbytes / 1e6:.0f} MB)",
+            "kernel": plan["kernel"]}
+
+
+class BenchFailure(RuntimeError):
+    pass
 
 
 def run_ours(args) -> None:
@@ -406,7 +465,7 @@ def run_ours(args) -> None:
     batches = [PackedBatch(p.packed_k, p.packed_v, p.scales_k, p.scales_v, p.valid_tokens,
                            w.bits, w.group_size) for p in pools]
     # N > 1: this rank's 1024 blocks are its token-block shard of the N x 1024-block context;
-    # the library's ShardedDecoder decodes it, all-gathers (out, lse) over NCCL and merges.
+    # the library's ShardedDecoder runs one fused decode + NVLink exchange kernel per rank.
     sharded = ShardedDecoder("tokens") if world > 1 else None
 
     def step(i: int):
@@ -418,13 +477,30 @@ def run_ours(args) -> None:
                    w.group_size, scale, out=out_v, lse=lse_v)
 
     stream = torch.cuda.current_stream(device)
-
     graphs = []  # CUDA graphs of timed steps; released before the process group is destroyed
+
+    def check_status(where: str) -> None:
+        """Every rank waits for its kernels and reads its device status word; any flagged
+        failure (on any rank) ends the run with an error instead of a number."""
+        torch.cuda.synchronize(device)
+        if sharded is not None:
+            sharded.check()  # collective: all ranks raise together
+            return
+        value = ops.read_device_status_all(device)
+        if value:
+            raise BenchFailure(f"{where}: device status {value:#x} "
+                               f"({ops.describe_status(value)})")
+
+    def barrier() -> None:
+        if dist:
+            dist.barrier()
 
     def timed(fn, steps: int, warmup: int, graph: bool = False) -> float:
         """Device time per step (max over ranks). graph=True captures the `steps` steps into one
         CUDA graph after the eager warm-up and replays it once more untimed before the timed
-        replay: the same kernels and collectives, without the per-launch host latency."""
+        replay: the same kernels and collectives, without the per-launch host latency. Every
+        rank runs exactly the same number of steps."""
+        barrier()
         for i in range(warmup):
             fn(i)
         run = None
@@ -443,8 +519,7 @@ def run_ours(args) -> None:
             graphs.append(g)
             g.replay()
             run = g.replay
-        if dist:
-            dist.barrier()
+        barrier()
         torch.cuda.synchronize(device)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -455,8 +530,7 @@ def run_ours(args) -> None:
                 fn(i)
         e1.record(stream)
         torch.cuda.synchronize(device)
-        if dist:
-            dist.barrier()
+        barrier()
         ms = e0.elapsed_time(e1) / steps
         if dist:
             t = torch.tensor([ms], device=device)
@@ -464,31 +538,37 @@ def run_ours(args) -> None:
             ms = float(t.item())
         return ms
 
-    def busy(seconds: float) -> None:
-        """Untimed steps that keep the GPU under the same load while clocks are sampled."""
-        t_end = time.perf_counter() + seconds
-        i = 0
-        while time.perf_counter() < t_end:
-            for _ in range(50):
+    def busy(calls: int) -> None:
+        """Untimed steps that keep the GPU under the same load while clocks are sampled: a
+        fixed number of calls, the same on every rank (each multi-GPU step is an exchange that
+        every rank must join), in batches of 50 with a synchronisation after each."""
+        barrier()
+        for start in range(0, calls, 50):
+            for i in range(start, min(calls, start + 50)):
                 step(i)
-                i += 1
             torch.cuda.synchronize(device)
+        barrier()
 
     # ---- device-timed whole step (inputs resident in HBM); clocks sampled around it
+    busy_calls = 0 if args.kernel_only else 20000  # ~1 s of decodes at ~45 us
     with ClockSampler(device.index) as clocks:
-        busy(0.0 if args.kernel_only else 1.0)
+        busy(busy_calls)
         ms = timed(step, args.steps, max(args.warmup, 3), graph=not args.eager)
-        busy(0.0 if args.kernel_only else 0.5)
+        busy(busy_calls // 2)
     clock_summary = clocks.summary()
+    check_status("timed decode steps")
     value = world * nbytes / (ms * 1e-3) / 1e9
     if args.kernel_only:
         torch.cuda.synchronize(device)
         graphs.clear()
+        if sharded is not None:
+            sharded.close()
         if dist:
             dist.destroy_process_group()
         if rank == 0:
             emit({"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
-                  "steps": args.steps, "ms_per_step": ms, "kernel_only": True, "path": args.path})
+                  "steps": args.steps, "ms_per_step": ms, "kernel_only": True, "path": args.path,
+                  "device_status": 0})
         return
 
     # ---- roofline leg: the dominant kernel alone on this rank, same inputs and rotation. The
@@ -516,6 +596,7 @@ def run_ours(args) -> None:
         kernel_ms = timed(local_decode, args.steps, 3, graph=not args.eager)
     else:
         kernel_ms = split_ms
+    check_status("roofline legs")
     kernel_name = {"tensor_core_tma": "tma_decode_kernel",
                    "tensor_core_stream": "async_decode_kernel",
                    "tensor_core_regs": "tc_decode_kernel",
@@ -528,6 +609,29 @@ def run_ours(args) -> None:
         tinfo = json.loads(tfile.read_text())
         if kernel_name in tinfo.get("kernel", ""):
             traffic = tinfo.get("dram_bytes_per_launch")
+
+    # ---- N > 1: every rank must hold the same result, equal to the ranks' local decodes
+    # merged by the NCCL path (all-gather + N-way merge kernel).
+    agree = None
+    if sharded is not None:
+        ox, lx = sharded.run(q, batches[0], scale)
+        ox, lx = ox.clone(), lx.clone()
+        torch.cuda.synchronize(device)
+        got = torch.empty((world, qh * d + qh), dtype=torch.float32, device=device)
+        dist.all_gather_into_tensor(got.view(-1), torch.cat([ox.view(-1), lx]))
+        same = all(torch.equal(got[r], got[0]) for r in range(world))
+        nccl = ShardedDecoder("tokens", transport="nccl")
+        on, ln = nccl.run(q, batches[0], scale)
+        finite = bool(torch.isfinite(ox).all()) and bool(torch.isfinite(lx).all())
+        diff = torch.tensor([float((on - ox).abs().max()), float((ln - lx).abs().max()),
+                             0.0 if finite else 1.0], device=device)
+        dist.all_reduce(diff, op=dist.ReduceOp.MAX)
+        agree = {"ranks_agree": bool(same), "exchange_vs_nccl_merge_max_abs_out": float(diff[0]),
+                 "exchange_vs_nccl_merge_max_abs_lse": float(diff[1]),
+                 "finite": bool(diff[2] == 0.0)}
+        check_status("rank agreement check")
+        if not same or diff[0] > 1e-5 or diff[1] > 1e-5 or diff[2] != 0.0:
+            raise BenchFailure(f"multi-GPU results disagree: {agree}")
 
     # ---- end to end through the plugin with host buffers (H2D + decode + D2H each step)
     backend = B200AttentionBackend()
@@ -550,19 +654,39 @@ def run_ours(args) -> None:
 
     e2e_steps = max(3, min(args.steps, 20))
     e2e_ms = timed(e2e_step, e2e_steps, 3)
+    if sharded is None:
+        backend.check(device)
+    check_status("end-to-end steps")
     e2e_value = world * nbytes / (e2e_ms * 1e-3) / 1e9
 
-    # ---- the reference's own entry point, KVSSDPipeline.decode(query, layer), from a store file
-    # of this rank's layer: native record reads (page cache), chunked host-to-device copies,
-    # on-GPU record decode (headers + CRC-32) and the fused decode; plus the GPU record decode
-    # alone on the layer's records resident in HBM.
-    pipeline = None
+    # ---- the c4 multi-layer step: KV-head sharded over the ranks (one batched launch over the
+    # rank's 32 layers + one NCCL all-gather of the output rows per step).
     c4 = None
-    small = None
+    if not args.no_c4:
+        c4_fn, c4_batch, c4_bytes = c4_step(w, base, device, rank, world, dist)
+        c4_ms = timed(c4_fn, max(3, min(args.steps, 20)), 3, graph=not args.eager)
+        if c4_batch.read_status():
+            raise BenchFailure("c4 batched decode flagged a device failure")
+        check_status("c4 steps")
+        total = 32 * (w.blocks_per_layer // 2) * w.bytes_per_block
+        c4 = {"workload": f"c4: 32 layers x 65536 tokens, INT4 g32, 8 KV heads, GQA 4; KV heads "
+                          f"sharded over {world} GPU(s) ({w.kv_heads // world} per GPU), one "
+                          "batched launch over the rank's 32 layers"
+                          + (" + one NCCL all-gather of all layers' output rows" if world > 1
+                             else "") + " per step (strong scaling: the step's work is fixed)",
+              "n_gpus": world, "us_per_step": c4_ms * 1e3, "us_per_layer": c4_ms * 1e3 / 32,
+              "GB/s": total / (c4_ms * 1e-3) / 1e9, "bytes_per_step": total,
+              "bytes_per_gpu": c4_bytes, "per_gpu_hbm_frac": c4_bytes / (c4_ms * 1e-3) / 1e9 / peak}
+        del c4_fn, c4_batch
+
+    # ---- the reference's own entry point, KVSSDPipeline.decode(query, layer), from a store file
+    # of this rank's layer, plus the GPU record decode alone; other single-GPU configurations.
+    pipeline = small = int2 = None
     if not args.no_pipeline and world == 1:
         pipeline = pipeline_legs(w, base, q, scale, device, rank, args)
-        c4 = c4_legs(w, base, device, args)
         small = small_config_legs(device)
+        int2 = int2_leg(device)
+        check_status("single-GPU legs")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -570,13 +694,13 @@ def run_ours(args) -> None:
     torch.cuda.synchronize(device)
     graphs.clear()  # graphs that hold NCCL calls go before the process group
     if sharded is not None:
-        sharded.close()  # collective: unmaps the peers' exchange buffers
+        sharded.close()  # collective: final status check, unmaps the peers' exchange buffers
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
-    launches_per_step = 1 if fused else 2 + (1 if world > 1 else 0)
+    launches_per_step = 1 if fused else 2
     record = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
@@ -611,16 +735,21 @@ def run_ours(args) -> None:
                          if world > 1 else "B200AttentionBackend.run (C ABI)")
                         + " from pinned host buffers"},
         "gpu_launches": args.steps * launches_per_step,
+        "device_status": 0,
         "clocks": clock_summary,
     }
+    if agree is not None:
+        record.update(agree)
     if cpu is not None:
         record["cpu_baseline"] = cpu
-    if pipeline is not None:
-        record["pipeline"] = pipeline
     if c4 is not None:
         record["c4_multi_layer"] = c4
+    if int2 is not None:
+        record["int2_128k"] = int2
     if small is not None:
         record["c1_c3_latency"] = small
+    if pipeline is not None:
+        record["pipeline"] = pipeline
     emit(record)
 
 
@@ -642,8 +771,16 @@ def main() -> None:
     os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args)
-    else:
+        return
+    try:
         run_ours(args)
+    except Exception as exc:  # a failed check prints no result line and exits non-zero
+        from kvssd_b200.ops import DeviceFailure
+
+        if isinstance(exc, (BenchFailure, DeviceFailure)):
+            print(f"bench failed: {exc}", file=sys.stderr)
+            raise SystemExit(3) from exc
+        raise
 
 
 if __name__ == "__main__":

@@ -115,6 +115,11 @@ KVSSD_B200_API int kvssd_b200_decode(const void* query, int query_dtype, const u
  * rejected with KVSSD_B200_ERR_WORKSPACE before anything is launched. The first call on each
  * device resolves the scratch address and zeroes its 2048-byte header (the only part
  * that must start at zero) on `stream`; make that first call before any stream capture.
+ * The address is kept per device and driver context: after cudaDeviceReset the next call
+ * (again before any capture) sets the new context's scratch up the same way. After a call
+ * that flagged a wait that gave up (status bits 4, 8 or 32), call kvssd_b200_read_status on
+ * the scratch with clear = 1: it re-zeroes the whole header, including the arrival counters
+ * a late CTA may have left behind.
  * Every call on a device uses the same scratch, so calls on one device must not overlap in
  * time (one stream, or events between streams): overlapping calls race on the parts.
  * If `scratch` is not NULL it receives the scratch address, which kvssd_b200_read_status
@@ -278,8 +283,13 @@ KVSSD_B200_API int kvssd_b200_decode_exchange(const void* query, int query_dtype
  * of range, 2 = valid_tokens entry out of [0, block_tokens], 4 = a fused combine gave up after
  * waiting about a second for the other CTAs' parts, 8 = a cross-GPU exchange gave up waiting
  * for another rank, 16 = a batched problem descriptor was refused, 32 = a TMA-fed kernel gave
- * up waiting for its copies; out/lse of a timed-out call are invalid). Returns
- * KVSSD_B200_ERR_DEVICE_STATUS when it is nonzero. No reference counterpart. */
+ * up waiting for its copies). After bits 4, 8 or 32 the kernels write NaN into out and lse of
+ * that call and of every later call on the workspace until the word is cleared, so a failure
+ * is never returned as a plausible number. clear = 1 with a nonzero word re-zeroes the
+ * workspace's whole 2048-byte header (status word and arrival counters), which makes the
+ * workspace usable again. Returns KVSSD_B200_ERR_DEVICE_STATUS when the word is nonzero. No
+ * reference counterpart (the reference raises through TORCH_CHECK,
+ * csrc/fused_decode.cu:141). */
 KVSSD_B200_API int kvssd_b200_read_status(void* workspace, int clear, unsigned* device_status,
                            kvssd_b200_stream_t stream);
 

@@ -3,6 +3,7 @@
 // Validation mirrors the reference's checks so a caller sees the same refusals:
 // PackedBatch.validate (src/kvssd/backends/base.py:29-55), the op bindings
 // (csrc/bindings.cpp:26-38) and the kernel launcher (csrc/fused_decode.cu:117-121).
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -36,7 +37,8 @@ using DequantKernel = void (*)(const uint8_t*, const __half*, long long, int, in
                                uint8_t*);
 DequantKernel dequant_kernel_for(int bits, int mode);
 
-__global__ void combine_parts_kernel(const float*, const float*, int, int, int, float*, float*);
+__global__ void combine_parts_kernel(const float*, const float*, int, int, int, float*, float*,
+                                     const unsigned*);
 __global__ void merge_chunks_kernel(const float*, const float*, int, int, int, float*, float*);
 __global__ void merge_pair_kernel(const float*, const float*, const float*, const float*, int,
                                   int, float*, float*);
@@ -234,7 +236,7 @@ int make_plan(const Geometry& g, bool aligned, bool allow_stream, Plan& p,
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 cudaError_t launch_combine(const float* part_acc, const float* part_ml, int n_parts, int qh, int d,
-                           float* out, float* lse, cudaStream_t s) {
+                           float* out, float* lse, const unsigned* status, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(qh, (d + 31) / 32, 1);
   cfg.blockDim = dim3(kCombineThreads, 1, 1);
@@ -246,7 +248,7 @@ cudaError_t launch_combine(const float* part_acc, const float* part_ml, int n_pa
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, combine_parts_kernel, part_acc, part_ml, n_parts, qh, d, out,
-                            lse);
+                            lse, status);
 }
 
 }  // namespace
@@ -409,7 +411,7 @@ int launch_decode(DecodeArgs& a, const Plan& p, float* out, float* lse, cudaStre
   }
   int st = launch_split(a, p, s);
   if (st) return st;
-  cudaError_t e = launch_combine(a.part_acc, a.part_ml, p.n_parts, a.qh, a.d, out, lse, s);
+  cudaError_t e = launch_combine(a.part_acc, a.part_ml, p.n_parts, a.qh, a.d, out, lse, a.status, s);
   return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "combine launch");
 }
 
@@ -510,26 +512,63 @@ __device__ __align__(256) unsigned char g_static_scratch[KVSSD_B200_STATIC_SCRAT
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
-void* g_scratch_ptr[kMaxDevices] = {};
+struct ScratchSlot {
+  unsigned long long context = 0;  // driver context id the address belongs to (0: none yet)
+  void* ptr = nullptr;
+};
+ScratchSlot g_scratch[kMaxDevices];
 
-// Address of the current device's scratch. The first call per device resolves the symbol
-// (with the device current) and zeroes the status header on `s`.
+// Unique id of the calling thread's current driver context (cuCtxGetCurrent + cuCtxGetId,
+// resolved once through the runtime, so the library needs no link against libcuda). A device
+// reset or a new primary context gives a new id; 0 when it cannot be determined.
+unsigned long long current_context_id() {
+  using GetCurrentFn = CUresult (*)(CUcontext*);
+  using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+  static const std::pair<GetCurrentFn, GetIdFn> fns = [] {
+    void* cur = nullptr;
+    void* id = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &cur, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess || q != cudaDriverEntryPointSuccess)
+      cur = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &id, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess || q != cudaDriverEntryPointSuccess)
+      id = nullptr;
+    return std::make_pair(reinterpret_cast<GetCurrentFn>(cur), reinterpret_cast<GetIdFn>(id));
+  }();
+  if (!fns.first || !fns.second) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long ident = 0;
+  if (fns.first(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (fns.second(ctx, &ident) != CUDA_SUCCESS) return 0;
+  return ident;
+}
+
+// Address of the current device's scratch. The first call per device and context resolves
+// the symbol (with the device current) and zeroes the status header on `s`; a later context
+// on the same device (after cudaDeviceReset) is a fresh module instance and is set up again.
 int static_scratch(cudaStream_t s, void** ptr) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices)
     return fail(KVSSD_B200_ERR_UNSUPPORTED, "static scratch supports device ordinals below 64");
+  // The runtime binds the device's primary context to this thread on its first call above.
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_ptr[dev] == nullptr) {
+  ScratchSlot& slot = g_scratch[dev];
+  if (slot.ptr == nullptr || ctx == 0 || slot.context != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "static scratch address");
-    e = cudaMemsetAsync(p, 0, kHeaderBytes, s);
-    if (e != cudaSuccess) return cuda_fail(e, "static scratch status clear");
-    g_scratch_ptr[dev] = p;
+    if (slot.ptr == nullptr || slot.context != ctx || p != slot.ptr) {
+      e = cudaMemsetAsync(p, 0, kHeaderBytes, s);
+      if (e != cudaSuccess) return cuda_fail(e, "static scratch status clear");
+    }
+    slot.ptr = p;
+    slot.context = ctx;
   }
-  *ptr = g_scratch_ptr[dev];
+  *ptr = slot.ptr;
   return KVSSD_B200_OK;
 }
 
@@ -593,6 +632,7 @@ int kvssd_b200_decode_combine(const void* workspace, int n_parts, int query_head
   const float* ml = reinterpret_cast<const float*>(static_cast<const char*>(workspace) + kHeaderBytes);
   const float* acc = ml + static_cast<size_t>(n_parts) * query_heads * 2;
   cudaError_t e = launch_combine(acc, ml, n_parts, query_heads, head_dim, out, lse,
+                                 static_cast<const unsigned*>(workspace),
                                  reinterpret_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "combine launch");
 }
@@ -910,7 +950,11 @@ int kvssd_b200_read_status(void* workspace, int clear, unsigned* device_status,
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return cuda_fail(e, "status read");
   if (clear && host) {
-    e = cudaMemsetAsync(workspace, 0, sizeof(unsigned), s);
+    // The whole header: after a timed-out wait, a CTA that arrived late may have left an
+    // arrival counter off zero, which would make the next call's combine start early. The
+    // stream has drained above, so no kernel of this workspace is running.
+    e = cudaMemsetAsync(workspace, 0, kHeaderBytes, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(e, "status clear");
   }
   *device_status = host;

@@ -42,12 +42,15 @@ __device__ __forceinline__ float block_reduce_sum(float v, float* red) {
 }
 
 // grid = (query_heads, ceil(d / 32)), block = 32 * kCombineWarps threads: one slice per CTA.
+// status: the decode's device status word; a fatal bit there (a split kernel that gave up
+// waiting for its copies) makes the result NaN.
 __global__ void __launch_bounds__(32 * kCombineWarps) combine_parts_kernel(
     const float* __restrict__ part_acc, const float* __restrict__ part_ml, int n_parts, int qh,
-    int d, float* __restrict__ out, float* __restrict__ lse) {
+    int d, float* __restrict__ out, float* __restrict__ lse, const unsigned* status) {
   // Parts are produced by the preceding decode grid (programmatic dependent launch).
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  combine_slice(part_acc, part_ml, n_parts, qh, d, blockIdx.x, blockIdx.y, out, lse);
+  const bool poison = (ld_acquire_gpu(status) & kDevFatalBits) != 0u;
+  combine_slice(part_acc, part_ml, n_parts, qh, d, blockIdx.x, blockIdx.y, out, lse, poison);
 }
 
 // grid = (query_heads, ceil(d / blockDim)); outs [n, qh, d], lses [n, qh].

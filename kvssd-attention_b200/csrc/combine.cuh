@@ -13,6 +13,13 @@ namespace kvb {
 constexpr int kCombineWarps = 16;   // the caller's block is 32 * kCombineWarps threads
 constexpr float kLn2 = 0.693147180559945309f;
 
+// Status bits after which a decode's result is not trustworthy: a wait gave up, so parts,
+// ring stages or another rank's slices may be missing. A combine that sees any of them in
+// the (sticky) status word writes NaN into out and lse instead of a plausible number, so the
+// failure reaches the caller through the result itself, without a host synchronisation.
+constexpr unsigned kDevFatalBits = kDevCombineTimeout | kDevExchangeTimeout | kDevStreamTimeout;
+__device__ __forceinline__ float nan_f32() { return __uint_as_float(0x7fffffffu); }
+
 // Warp w folds the contiguous part range [w*n/W, (w+1)*n/W) for dims [32*chunk, 32*chunk+32),
 // 32 parts per batch: all of a batch's loads (lane j: part j's m and l; every lane: its dim of
 // the 32 parts' rows) are issued before any of them is used, so a batch costs one round trip
@@ -92,27 +99,29 @@ __device__ __forceinline__ void combine_slice_result(const float* __restrict__ p
 }
 
 // The slice's normalised output and natural-log LSE written to out [qh, d] / lse [qh].
+// poison: write NaN instead (see kDevFatalBits).
 __device__ __forceinline__ void combine_slice(const float* __restrict__ part_acc,
                                               const float* __restrict__ part_ml, int n_parts,
                                               int qh, int d, int h, int chunk,
-                                              float* __restrict__ out, float* __restrict__ lse) {
+                                              float* __restrict__ out, float* __restrict__ lse,
+                                              bool poison) {
   float o = 0.f, l2 = -INFINITY;
   combine_slice_result(part_acc, part_ml, n_parts, qh, d, h, chunk, &o, &l2);
   const int lane = threadIdx.x & 31, dd = chunk * 32 + lane;
   if (threadIdx.x < 32) {
-    if (dd < d) out[static_cast<size_t>(h) * d + dd] = o;
-    if (chunk == 0 && lane == 0) lse[h] = l2 * kLn2;
+    if (dd < d) out[static_cast<size_t>(h) * d + dd] = poison ? nan_f32() : o;
+    if (chunk == 0 && lane == 0) lse[h] = poison ? nan_f32() : l2 * kLn2;
   }
 }
 
 // One warp folds all n_parts (<= 32) parts of a slice: lane j loads part j's m and l, every
 // lane its dim of each part's row (all loads issued before use), then the weights reach the
-// lanes by shuffle. Writes the slice's normalised output and natural-log LSE.
+// lanes by shuffle. Writes the slice's normalised output and natural-log LSE (NaN: poison).
 __device__ __forceinline__ void combine_slice_warp(const float* __restrict__ part_acc,
                                                    const float* __restrict__ part_ml,
                                                    int n_parts, int qh, int d, int h, int chunk,
                                                    float* __restrict__ out,
-                                                   float* __restrict__ lse) {
+                                                   float* __restrict__ lse, bool poison) {
   const int lane = threadIdx.x & 31;
   const int dd = chunk * 32 + lane;
   const bool has_dim = dd < d;
@@ -139,8 +148,9 @@ __device__ __forceinline__ void combine_slice_warp(const float* __restrict__ par
 #pragma unroll
   for (int j = 0; j < 32; ++j) t = fmaf(__shfl_sync(0xffffffffu, wp, j), v[j], t);
   const bool empty = (mx == -INFINITY) || !(ls > 0.f);
-  if (has_dim) out[static_cast<size_t>(h) * d + dd] = empty ? 0.f : t / ls;
-  if (chunk == 0 && lane == 0) lse[h] = empty ? -INFINITY : (mx + log2f(ls)) * kLn2;
+  if (has_dim) out[static_cast<size_t>(h) * d + dd] = poison ? nan_f32() : empty ? 0.f : t / ls;
+  if (chunk == 0 && lane == 0)
+    lse[h] = poison ? nan_f32() : empty ? -INFINITY : (mx + log2f(ls)) * kLn2;
 }
 
 }  // namespace kvb

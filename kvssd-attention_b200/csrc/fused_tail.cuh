@@ -24,9 +24,12 @@ constexpr unsigned kCombineMaxPolls = 1u << 26;
 // Two buffer halves suffice, since a rank can only be one epoch ahead of the slowest reader.
 // The epoch is kept on the device (the buffer's header), so a call captured in a CUDA graph
 // gets a fresh epoch on every replay.
+// poison: this rank's slice is not trustworthy (see kDevFatalBits); it is pushed as NaN, so
+// every rank's merged slice becomes NaN. A lane whose wait gives up poisons the whole slice.
 template <int D>
 __device__ __forceinline__ void exchange_slice(const DecodeArgs& a, unsigned epoch, int slice,
-                                               int n_slices, float o, float l2) {
+                                               int n_slices, float o, float l2, bool poison) {
+  if (poison) o = l2 = nan_f32();
   const int lane = threadIdx.x & 31;
   const int world = a.xworld, par = static_cast<int>(epoch & 1u);
   const unsigned long long tag = static_cast<unsigned long long>(epoch) << 32;
@@ -81,8 +84,10 @@ __device__ __forceinline__ void exchange_slice(const DecodeArgs& a, unsigned epo
   constexpr int kChunks = (D + 31) / 32;
   const int h = slice / kChunks, chunk = slice % kChunks, dd = chunk * 32 + lane;
   const bool empty = M == -INFINITY || !(den > 0.f);
-  if (dd < D) a.out[static_cast<size_t>(h) * D + dd] = empty ? 0.f : num / den;
-  if (chunk == 0 && lane == 0) a.lse[h] = empty ? -INFINITY : (M + log2f(den)) * kLn2;
+  const bool bad = __any_sync(0xffffffffu, timed_out) || poison;
+  if (dd < D) a.out[static_cast<size_t>(h) * D + dd] = bad ? nan_f32() : empty ? 0.f : num / den;
+  if (chunk == 0 && lane == 0)
+    a.lse[h] = bad ? nan_f32() : empty ? -INFINITY : (M + log2f(den)) * kLn2;
 }
 
 // Fused split-KV combine at the end of the decode grid (launched cooperatively, so all CTAs
@@ -92,10 +97,14 @@ __device__ __forceinline__ void exchange_slice(const DecodeArgs& a, unsigned epo
 // more slices each. Each combiner counts itself on tickets[1] as soon as it has seen every
 // arrival -- the atomic's round trip overlaps its fold -- and the last one re-arms both
 // counters (zero again for the next call) and publishes the exchange epoch after its fold.
-// The wait is bounded: on timeout the CTA flags kDevCombineTimeout and carries on.
+// The wait is bounded: on timeout the CTA flags kDevCombineTimeout and carries on. A combiner
+// that timed out, or that finds a fatal bit in the status word once every part has arrived
+// (another CTA gave up on its copies, or an earlier call on this workspace failed and nobody
+// has cleared the word), writes NaN into its slices of out and lse.
 template <int D>
 __device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned epoch,
                                                    int n_parts) {
+  __shared__ int poison_flag;
   __syncthreads();  // every warp's part stores precede the CTA's release below
   constexpr int kChunks = (D + 31) / 32;
   const int n_slices = a.qh * kChunks;
@@ -106,17 +115,24 @@ __device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned
     if (k >= 0) {
       const unsigned long long t0 = global_ns();
       unsigned polls = 0;
-      while (ld_acquire_gpu(a.tickets) < static_cast<unsigned>(a.n_splits)) {
+      bool timed_out = false;
+      // Signed: a counter left below zero (a corrupted workspace header) reads as "parts
+      // missing" to every combiner, so all of them wait out the bound and fail closed together
+      // instead of some folding early.
+      while (static_cast<int>(ld_acquire_gpu(a.tickets)) < a.n_splits) {
         if (++polls > kCombineMaxPolls || global_ns() - t0 > kCombineWaitNs) {
           atomicOr(a.status, kDevCombineTimeout);
+          timed_out = true;
           break;
         }
         __nanosleep(32);
       }
+      poison_flag = timed_out || (ld_acquire_gpu(a.status) & kDevFatalBits) != 0u;
     }
   }
   if (k < 0) return;
   __syncthreads();
+  const bool poison = poison_flag != 0;
   // Every combiner has passed its wait when tickets[1] reaches n_comb; the returned count is
   // only needed after the fold.
   unsigned combined_before = 0u;
@@ -129,19 +145,19 @@ __device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned
     for (int j = warp; j < mine; j += n_warps) {
       const int sl = k + j * n_comb;
       combine_slice_warp(a.part_acc, a.part_ml, n_parts, a.qh, D, sl / kChunks, sl % kChunks,
-                         a.out, a.lse);
+                         a.out, a.lse, poison);
     }
     __syncthreads();
   } else {
   for (int sl = k; sl < n_slices; sl += n_comb) {
     if (a.xworld == 0) {
       combine_slice(a.part_acc, a.part_ml, n_parts, a.qh, D, sl / kChunks, sl % kChunks,
-                    a.out, a.lse);
+                    a.out, a.lse, poison);
     } else {
       float o = 0.f, l2 = -INFINITY;
       combine_slice_result(a.part_acc, a.part_ml, n_parts, a.qh, D, sl / kChunks,
                            sl % kChunks, &o, &l2);
-      if (threadIdx.x < 32) exchange_slice<D>(a, epoch, sl, n_slices, o, l2);
+      if (threadIdx.x < 32) exchange_slice<D>(a, epoch, sl, n_slices, o, l2, poison);
     }
   }
   }

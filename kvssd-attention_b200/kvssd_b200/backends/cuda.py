@@ -43,12 +43,22 @@ class B200AttentionBackend:
     def run(
         self, query: torch.Tensor, batch: PackedBatch, sm_scale: float
     ) -> tuple[torch.Tensor, torch.Tensor]:
+        """(out fp32 [QH, D], lse fp32 [QH]) on the current stream, without synchronising.
+
+        Kernel failures surface the way the reference's TORCH_CHECK does, as an exception,
+        but without a host synchronisation per call: the call's device status word is copied
+        into pinned memory after its kernels, and the next ``run`` on the same stream (or
+        ``check``) raises ops.DeviceFailure (a RuntimeError) if that word flagged a failure.
+        The failed call's own out/lse are NaN, so nothing plausible is returned meanwhile.
+        """
         PackedBatch.validate(batch, query)
         if query.device.type != "cuda":
             raise RuntimeError(f"CUDA extension requires a CUDA device, got {query.device.type}")
         if not _native.available():
             raise RuntimeError("CUDA extension unavailable; run `python -m kvssd_b200._build`")
-        return ops.decode(
+        watch = ops.status_watch(query.device)
+        watch.poll("B200AttentionBackend.run (an earlier call)")
+        result = ops.decode(
             query,
             batch.packed_k.contiguous(),
             batch.packed_v.contiguous(),
@@ -59,3 +69,12 @@ class B200AttentionBackend:
             batch.group_size,
             sm_scale,
         )
+        watch.arm("B200AttentionBackend.run")
+        return result
+
+    def check(self, device: torch.device | str | None = None) -> None:
+        """Waits for this stream's outstanding status reads and raises ops.DeviceFailure if
+        any call on it flagged a failure."""
+        device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        ops.status_watch(device).check("B200AttentionBackend.run")

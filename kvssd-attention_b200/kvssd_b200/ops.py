@@ -208,7 +208,11 @@ class BatchedDecode:
     tensors the descriptors point to may be refilled in place between replays).
     """
 
-    def __init__(self, problems, bits: int, group_size: int, sm_scale: float):
+    def __init__(self, problems, bits: int, group_size: int, sm_scale: float,
+                 out: torch.Tensor | None = None, lse: torch.Tensor | None = None):
+        """``out`` fp32 [L, QH, D] / ``lse`` fp32 [L, QH] (optional): contiguous buffers the
+        L problems write into (e.g. one buffer to all-gather across ranks); allocated per
+        problem when absent."""
         problems = list(problems)
         if not problems:
             raise ValueError("at least one problem is required")
@@ -228,8 +232,19 @@ class BatchedDecode:
         bt, qh, kvh, d, qdtype, device = geom0
         self.device = device
         self._keep = checked  # the tensors the descriptors point to
-        self.outs = [(torch.empty((qh, d), dtype=torch.float32, device=device),
-                      torch.empty((qh,), dtype=torch.float32, device=device)) for _ in checked]
+        n = len(checked)
+        if (out is None) != (lse is None):
+            raise ValueError("pass both out and lse, or neither")
+        if out is None:
+            self.outs = [(torch.empty((qh, d), dtype=torch.float32, device=device),
+                          torch.empty((qh,), dtype=torch.float32, device=device))
+                         for _ in checked]
+        else:
+            if tuple(out.shape) != (n, qh, d) or tuple(lse.shape) != (n, qh):
+                raise ValueError(f"out/lse must be [{n}, {qh}, {d}] and [{n}, {qh}]")
+            _require_cuda("out", out, device, torch.float32)
+            _require_cuda("lse", lse, device, torch.float32)
+            self.outs = [(out[i], lse[i]) for i in range(n)]
         desc = torch.empty((len(checked), 10), dtype=torch.int64, pin_memory=True)
         for i, ((query, kp, vp, ks, vs, valid, table, n_pool, n_sel), (out, lse)) in enumerate(
                 zip(checked, self.outs)):
@@ -360,17 +375,19 @@ def decode_combine(workspace: torch.Tensor, n_parts: int, query_heads: int, head
     return out, lse
 
 
-def read_device_status(device: torch.device | str | None = None, clear: bool = True) -> int:
-    """Synchronously reads the sticky device status word of the current stream's workspace.
+def read_device_status(device: torch.device | str | None = None, clear: bool = True,
+                       stream: torch.cuda.Stream | None = None) -> int:
+    """Synchronously reads the sticky device status word of the current (or given) stream's
+    workspace; ``clear`` re-zeroes the workspace header when the word is nonzero.
 
     Bit 1: a block-table entry was outside the pool; bit 2: a valid_tokens entry was outside
     [0, block_tokens] (such entries are skipped/clamped by the kernels, never dereferenced);
     bit 4: a fused combine, bit 8: a cross-GPU exchange, bit 32: a TMA-fed kernel's copy
-    wait gave up (about a second) -- the out/lse of that call are invalid; bit 16: a batched
-    problem descriptor was refused.
+    wait gave up (about a second) -- the out/lse of that call, and of later calls until the
+    word is cleared, are NaN; bit 16: a batched problem descriptor was refused.
     """
     device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    stream = torch.cuda.current_stream(device)
+    stream = stream or torch.cuda.current_stream(device)
     ws = _workspaces.get(device, stream, _WORKSPACE_HEADER)
     value = ctypes.c_uint()
     with torch.cuda.device(device):
@@ -380,6 +397,144 @@ def read_device_status(device: torch.device | str | None = None, clear: bool = T
     if status not in (_native.OK, _native.ERR_DEVICE_STATUS):
         _native.check(status, "kvssd_b200_read_status")
     return int(value.value)
+
+
+def read_device_status_all(device: torch.device | str | None = None, clear: bool = True) -> int:
+    """OR of the status words of every decode workspace on ``device`` (one per stream that has
+    decoded, graph-capture streams included), read after synchronising the device."""
+    device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    torch.cuda.synchronize(device)
+    with _workspaces._lock:
+        buffers = [buf for (dev, _), buf in _workspaces._buffers.items() if dev == device.index]
+    total = 0
+    stream = torch.cuda.current_stream(device)
+    with torch.cuda.device(device):
+        for ws in buffers:
+            value = ctypes.c_uint()
+            status = _native.library().kvssd_b200_read_status(
+                _ptr(ws), 1 if clear else 0, ctypes.byref(value), stream.cuda_stream)
+            if status not in (_native.OK, _native.ERR_DEVICE_STATUS):
+                _native.check(status, "kvssd_b200_read_status")
+            total |= int(value.value)
+    return total
+
+
+# Status bits that make a call's result invalid (the kernels then write NaN into out/lse) or
+# that mean the caller passed entries the kernels had to refuse. Bit 2 (a valid_tokens entry
+# outside [0, block_tokens], clamped like kvssd's CPU path clamps it by slicing) is not one.
+FAILURE_BITS = (_native.DEV_BAD_BLOCK | _native.DEV_COMBINE_TIMEOUT |
+                _native.DEV_EXCHANGE_TIMEOUT | _native.DEV_BAD_PROBLEM |
+                _native.DEV_STREAM_TIMEOUT)
+
+_STATUS_TEXT = {
+    _native.DEV_BAD_BLOCK: "a block-table entry outside the pool",
+    _native.DEV_BAD_VALID: "a valid_tokens entry outside [0, block_tokens]",
+    _native.DEV_COMBINE_TIMEOUT: "the fused split-KV combine gave up waiting for parts",
+    _native.DEV_EXCHANGE_TIMEOUT: "the cross-GPU exchange gave up waiting for another rank",
+    _native.DEV_BAD_PROBLEM: "a batched problem descriptor was refused",
+    _native.DEV_STREAM_TIMEOUT: "a TMA-fed kernel gave up waiting for its copies",
+}
+
+
+def describe_status(value: int) -> str:
+    """Human-readable list of the conditions in a device status word."""
+    parts = [text for bit, text in _STATUS_TEXT.items() if value & bit]
+    return "; ".join(parts) or "none"
+
+
+# Bits after which the kernels write NaN into out/lse (a wait gave up).
+NAN_BITS = _native.DEV_COMBINE_TIMEOUT | _native.DEV_EXCHANGE_TIMEOUT | _native.DEV_STREAM_TIMEOUT
+
+
+class DeviceFailure(RuntimeError):
+    """A decode kernel flagged a failure in its workspace status word (see FAILURE_BITS)."""
+
+    def __init__(self, status: int, where: str):
+        self.status = status
+        tail = ("; the out/lse of the failed call are NaN" if status & NAN_BITS else
+                "; the offending entries were skipped, never dereferenced")
+        super().__init__(f"{where}: device status {status:#x} ({describe_status(status)}){tail}")
+
+
+class _StatusWatch:
+    """Asynchronous reads of one (device, stream) workspace's status word.
+
+    ``arm()`` enqueues, after a call's kernels, a 4-byte copy of the status word into a slot of
+    pinned host memory and records an event; ``poll()`` looks at the slots whose event has
+    completed (no synchronisation) and ``check()`` waits for all of them. A failure is raised
+    once, as DeviceFailure, after the word has been read and cleared on the device (which
+    re-zeroes the workspace header and makes the workspace usable again).
+    """
+
+    SLOTS = 4
+
+    def __init__(self, device: torch.device, stream: torch.cuda.Stream):
+        self.device, self.stream = device, stream
+        self._host = torch.zeros(self.SLOTS, dtype=torch.int32, pin_memory=True)
+        self._events: list[torch.cuda.Event | None] = [None] * self.SLOTS
+        self._next = 0
+
+    def _take(self, i: int, block: bool) -> int:
+        ev = self._events[i]
+        if ev is None:
+            return 0
+        if not block and not ev.query():
+            return 0
+        ev.synchronize()
+        self._events[i] = None
+        return int(self._host[i])
+
+    def _raise(self, value: int, where: str) -> None:
+        if value & FAILURE_BITS:
+            read_device_status(self.device, clear=True, stream=self.stream)
+            for i in range(self.SLOTS):  # older slots hold the same sticky bits
+                self._events[i] = None
+            raise DeviceFailure(value, where)
+
+    def arm(self, where: str) -> None:
+        if torch.cuda.is_current_stream_capturing():
+            return  # inside a graph capture the caller checks after replay (check())
+        i = self._next % self.SLOTS
+        self._raise(self._take(i, block=True), where)  # the slot's earlier read, long done
+        ws = _workspaces.get(self.device, self.stream, _WORKSPACE_HEADER)
+        with torch.cuda.stream(self.stream):
+            self._host[i:i + 1].copy_(ws[:4].view(torch.int32), non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(self.stream)
+        self._events[i] = ev
+        self._next += 1
+
+    def poll(self, where: str) -> None:
+        value = 0
+        for i in range(self.SLOTS):
+            value |= self._take(i, block=False)
+        self._raise(value, where)
+
+    def check(self, where: str) -> None:
+        value = 0
+        for i in range(self.SLOTS):
+            value |= self._take(i, block=True)
+        self._raise(value, where)
+
+    def discard(self) -> None:
+        """Waits for the outstanding reads and drops them (the caller reads the word itself)."""
+        for i in range(self.SLOTS):
+            self._take(i, block=True)
+
+
+_watch_lock = threading.Lock()
+_watches: dict[tuple[int, int], _StatusWatch] = {}
+
+
+def status_watch(device: torch.device, stream: torch.cuda.Stream | None = None) -> _StatusWatch:
+    """The status watch of ``device``'s current (or given) stream workspace."""
+    stream = stream or torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
+    with _watch_lock:
+        w = _watches.get(key)
+        if w is None:
+            w = _watches[key] = _StatusWatch(device, stream)
+        return w
 
 
 def decode_path(head_dim: int, bits: int, group_size: int) -> int:

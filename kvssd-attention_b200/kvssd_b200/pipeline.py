@@ -21,7 +21,9 @@ import math
 import torch
 
 from . import ops
-from .backends import AttentionBackend, resolve_attention_backend
+from .attention import select_backend
+from .backends import AttentionBackend, PackedBatch
+from .backends.cuda import B200AttentionBackend
 from .selectors import AllBlocks, BlockSelector
 
 
@@ -54,10 +56,8 @@ class KVSSDPipeline:
             raise ValueError("io_depth must be positive")
         if stage_blocks < 1:
             raise ValueError("stage_blocks must be positive")
-        if require_cuda_kernel and attention_backend not in (None, "auto", "cuda"):
-            raise ValueError("require_cuda_kernel conflicts with a non-CUDA attention backend")
-        requested = "cuda" if require_cuda_kernel else attention_backend
-        self.attention_backend = resolve_attention_backend(requested, self.device)
+        self.attention_backend = select_backend(self.device, require_cuda_kernel,
+                                                attention_backend)
         self.io_depth = io_depth
         self.stage_blocks = stage_blocks
         self.require_cuda_kernel = require_cuda_kernel
@@ -99,8 +99,8 @@ class KVSSDPipeline:
             with torch.cuda.stream(self.compute_stream):
                 self.compute_stream.wait_event(chunk.copied)
                 kp, vp, ks, vs, valid, status = ops.decode_records(dev, spec, layer, ids[lo:hi])
-                ops.decode(query, kp, vp, ks, vs, valid, spec.bits, spec.group_size, scale,
-                           out=outs[ci], lse=lses[ci])
+                self._attend(query, PackedBatch(kp, vp, ks, vs, valid, spec.bits,
+                                                spec.group_size), scale, outs[ci], lses[ci])
                 statuses[lo:hi].copy_(status)
                 dev.record_stream(self.compute_stream)
         with torch.cuda.stream(self.compute_stream):
@@ -113,7 +113,30 @@ class KVSSDPipeline:
         caller.wait_event(done)
         out.record_stream(caller)
         self._raise_on_bad_records(statuses, selected, layer)
+        if self._native:
+            watch = ops.status_watch(self.device, self.compute_stream)
+            with torch.cuda.stream(self.compute_stream):
+                watch.arm("KVSSDPipeline.decode")
+            watch.check("KVSSDPipeline.decode")  # the record statuses above already waited
         return out.to(query.dtype)
+
+    @property
+    def _native(self) -> bool:
+        return type(self.attention_backend) is B200AttentionBackend
+
+    def _attend(self, query: torch.Tensor, batch: PackedBatch, scale: float, out: torch.Tensor,
+                lse: torch.Tensor) -> None:
+        """One chunk's attention into (out, lse) through the resolved backend, as kvssd's
+        streamed pipeline calls backend.run per chunk (src/kvssd/pipeline.py:138-145). The
+        built-in ``cuda`` backend writes straight into the chunk's rows; another backend's
+        result is copied there."""
+        if self._native:
+            ops.decode(query, batch.packed_k, batch.packed_v, batch.scales_k, batch.scales_v,
+                       batch.valid_tokens, batch.bits, batch.group_size, scale, out=out, lse=lse)
+            return
+        o, l = self.attention_backend.run(query, batch, scale)
+        out.copy_(o)
+        lse.copy_(l)
 
     @staticmethod
     def _raise_on_bad_records(statuses: torch.Tensor, selected: list[int], layer: int) -> None:

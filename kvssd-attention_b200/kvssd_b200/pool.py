@@ -125,11 +125,24 @@ class DeviceBlockPool:
     def decode_table(self, query: torch.Tensor, table: torch.Tensor | None,
                      sm_scale: float | None = None, out: torch.Tensor | None = None,
                      lse: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-        """(out fp32, lse fp32) over the pool slots in ``table`` (None = every slot)."""
+        """(out fp32, lse fp32) over the pool slots in ``table`` (None = every slot).
+
+        Asynchronous; a kernel failure (a table entry outside the pool, a wait that gave up)
+        makes that call's result NaN and raises ops.DeviceFailure on the next decode on this
+        stream or on ``check()``."""
         scale = sm_scale if sm_scale is not None else 1.0 / math.sqrt(query.shape[-1])
-        return ops.decode(query, self.packed_k, self.packed_v, self.scales_k, self.scales_v,
-                          self.valid_tokens, self.spec.bits, self.spec.group_size, scale,
-                          block_table=table, out=out, lse=lse)
+        watch = ops.status_watch(self.device)
+        watch.poll("DeviceBlockPool.decode (an earlier call)")
+        result = ops.decode(query, self.packed_k, self.packed_v, self.scales_k, self.scales_v,
+                            self.valid_tokens, self.spec.bits, self.spec.group_size, scale,
+                            block_table=table, out=out, lse=lse)
+        watch.arm("DeviceBlockPool.decode")
+        return result
+
+    def check(self) -> None:
+        """Waits for the outstanding status reads of this device's current stream and raises
+        ops.DeviceFailure if a decode flagged a failure."""
+        ops.status_watch(self.device).check("DeviceBlockPool.decode")
 
     def decode(self, query: torch.Tensor, selector: BlockSelector | None = None,
                sm_scale: float | None = None) -> tuple[torch.Tensor, torch.Tensor]:

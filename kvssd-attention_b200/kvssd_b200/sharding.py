@@ -190,6 +190,7 @@ class ShardedDecoder:
         self._recv: torch.Tensor | None = None
         self._peer: PeerExchange | None = None
         self._peer_out: tuple[torch.Tensor, torch.Tensor] | None = None
+        self._device: torch.device | None = None  # the device of the last run
 
     def _use_peer(self, query: torch.Tensor, local: PackedBatch) -> bool:
         """Token shards on CUDA with a native streaming kernel (INT4 or INT2, head_dim 128, group
@@ -210,11 +211,49 @@ class ShardedDecoder:
             raise RuntimeError("peer transport needs the streaming kernel's shapes and alignment")
         return ok
 
+    def check(self) -> None:
+        """Collective failure check: every rank of the group calls it at the same point.
+
+        Each rank waits for its decodes, reads and clears the status words of its device's
+        decode workspaces (graph-capture streams included), and the ranks all-gather them. If any rank flagged a failure (a wait that gave up: the
+        exchange, the fused combine or a TMA copy; or a refused block-table entry), every rank
+        re-zeroes the peer-exchange buffers (after a rank missed a call the ranks' call numbers
+        differ, so later calls could never meet) and raises ops.DeviceFailure with the OR of
+        the words. A failed step has already returned NaN on every rank that ran it (the
+        exchange spreads a NaN slice to all ranks); ``run`` itself never raises on a device
+        failure, since a rank that stopped alone would leave the others' next exchange
+        without a partner.
+        """
+        from . import ops
+
+        device = self._device
+        value = 0
+        if device is not None and device.type == "cuda":
+            ops.status_watch(device).discard()
+            value = ops.read_device_status_all(device, clear=True)
+        words = [0] * self.world
+        if self.world > 1:
+            dist.all_gather_object(words, value, group=self.group)
+        else:
+            words = [value]
+        total = 0
+        for w in words:
+            total |= int(w)
+        if total & ops.FAILURE_BITS:
+            if self._peer is not None:
+                self._peer.reset()
+            bad = [r for r, w in enumerate(words) if int(w) & ops.FAILURE_BITS]
+            raise ops.DeviceFailure(total, f"ShardedDecoder (ranks {bad} flagged)")
+
     def close(self) -> None:
-        """Releases the peer-exchange buffers (collective when the peer transport was used)."""
-        if self._peer is not None:
-            self._peer.close()
-            self._peer = None
+        """Checks the group for device failures (``check``) and releases the peer-exchange
+        buffers; collective. The buffers are released even when the check raises."""
+        try:
+            self.check()
+        finally:
+            if self._peer is not None:
+                self._peer.close()
+                self._peer = None
 
     @property
     def world(self) -> int:
@@ -266,6 +305,7 @@ class ShardedDecoder:
     def run(self, query: torch.Tensor, local: PackedBatch,
             sm_scale: float) -> tuple[torch.Tensor, torch.Tensor]:
         qh, d = query.shape
+        self._device = query.device
         if self.mode == "heads":
             kvh_local = local.packed_k.shape[2]
             world = self.world

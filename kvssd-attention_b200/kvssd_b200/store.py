@@ -15,10 +15,33 @@ from pathlib import Path
 import torch
 
 from .format import BlockEntry, CacheSpec, Manifest, PackedKVBlock, decode_record, encode_record
-from .quant import quantize_tensor
+from .quant import QuantizedTensor, quantize_tensor
 
 DATA_FILE = "blocks.kvssd"
 MANIFEST_FILE = "manifest.json"
+
+
+def _quantized_blocks(keys: torch.Tensor, values: torch.Tensor, spec: CacheSpec):
+    """Yields the PackedKVBlocks of every (layer, block) in store order, one layer of keys and
+    values quantized at a time."""
+    layers, tokens = keys.shape[0], keys.shape[1]
+    bt = spec.block_tokens
+    n_blocks = -(-tokens // bt)
+    block_shape = (bt, spec.kv_heads, spec.head_dim)
+
+    def whole_blocks(x: torch.Tensor) -> QuantizedTensor:
+        padded = torch.zeros((n_blocks * bt, spec.kv_heads, spec.head_dim), dtype=x.dtype)
+        padded[:tokens].copy_(x.cpu())
+        return quantize_tensor(padded.view(n_blocks, *block_shape), spec.bits, spec.group_size)
+
+    def part(q: QuantizedTensor, b: int) -> QuantizedTensor:
+        return QuantizedTensor(q.packed[b], q.scales[b], block_shape, spec.bits, spec.group_size)
+
+    for layer in range(layers):
+        kq, vq = whole_blocks(keys[layer]), whole_blocks(values[layer])
+        for b in range(n_blocks):
+            valid = min(bt, tokens - b * bt)
+            yield PackedKVBlock(layer, b, valid, part(kq, b), part(vq, b))
 
 
 class _PreadFile:
@@ -87,40 +110,23 @@ class KVCacheStore:
         """Creates a store from [layers, tokens, kv_heads, head_dim] tensors.
 
         Tokens are cut into blocks of ``block_tokens``; the last block of a layer is
-        zero-padded and records its valid row count (src/kvssd/store.py:27-67).
+        zero-padded and records its valid row count (the contract of src/kvssd/store.py:27-67).
+        Each layer is quantized in one call: its token axis is zero-padded to whole blocks and
+        viewed as [blocks, block_tokens, kv_heads, head_dim]; the quantization groups lie along
+        head_dim, so this equals quantizing block by block. Records are then encoded from
+        per-block views of the result and written by ``from_blocks``.
         """
         spec.validate()
         if keys.shape != values.shape or keys.ndim != 4:
             raise ValueError("keys and values must share [layers,tokens,kv_heads,head_dim]")
         if keys.shape[0] != spec.layers or tuple(keys.shape[2:]) != (spec.kv_heads, spec.head_dim):
             raise ValueError("input tensors do not match CacheSpec")
-        root = Path(root)
-        root.mkdir(parents=True, exist_ok=True)
-        shape = (spec.block_tokens, spec.kv_heads, spec.head_dim)
-        entries: list[BlockEntry] = []
-        with (root / DATA_FILE).open("wb") as out:
-            for layer in range(spec.layers):
-                for block_id, start in enumerate(range(0, keys.shape[1], spec.block_tokens)):
-                    valid = min(spec.block_tokens, keys.shape[1] - start)
-                    k = torch.zeros(shape, dtype=keys.dtype)
-                    v = torch.zeros(shape, dtype=values.dtype)
-                    k[:valid].copy_(keys[layer, start : start + valid].cpu())
-                    v[:valid].copy_(values[layer, start : start + valid].cpu())
-                    block = PackedKVBlock(
-                        layer, block_id, valid,
-                        quantize_tensor(k, spec.bits, spec.group_size),
-                        quantize_tensor(v, spec.bits, spec.group_size),
-                    )
-                    record, crc = encode_record(block, spec)
-                    offset = out.tell()
-                    out.write(record)
-                    entries.append(BlockEntry(layer, block_id, offset, len(record), valid, crc))
-        manifest = Manifest(spec=spec, entries=entries)
-        manifest.save(root / MANIFEST_FILE)
-        return cls(root, manifest, storage_backend)
+        return cls.from_blocks(root, spec, _quantized_blocks(keys, values, spec),
+                               storage_backend)
 
     @classmethod
-    def from_blocks(cls, root: str | Path, spec: CacheSpec, blocks) -> "KVCacheStore":
+    def from_blocks(cls, root: str | Path, spec: CacheSpec, blocks,
+                    storage_backend: str | None = None) -> "KVCacheStore":
         """Writes already-quantized PackedKVBlocks (any order of (layer, block)) as a store in
         the same byte format as ``create``."""
         spec.validate()
@@ -136,7 +142,7 @@ class KVCacheStore:
                                           block.valid_tokens, crc))
         manifest = Manifest(spec=spec, entries=entries)
         manifest.save(root / MANIFEST_FILE)
-        return cls(root, manifest)
+        return cls(root, manifest, storage_backend)
 
     @classmethod
     def open(cls, root: str | Path, storage_backend: str | None = None) -> "KVCacheStore":

@@ -1,7 +1,9 @@
 """The streaming kernel's fused split-KV combine: equality with the two-launch path, the
 arrival counters returning to zero, and the bounded wait (a planted counter value that can
 never be reached makes the combining CTAs give up after about a second and flag status bit 4;
-nothing faults or hangs)."""
+nothing faults or hangs). A call that gave up returns NaN, later calls on the workspace return
+NaN until the status word is cleared, and the public entry points (the ``cuda`` backend's run,
+DeviceBlockPool) raise ops.DeviceFailure on the next call instead of returning a number."""
 
 from __future__ import annotations
 
@@ -87,14 +89,19 @@ def test_fused_combine_equals_two_launch_combine_and_resets_counters(layer):
 def test_fused_combine_wait_is_bounded_and_flagged(layer):
     w, t = layer
     ws = _workspace(w, t)
-    # Planted arrival count 2^32 - 100: after every CTA arrives the counter has wrapped to a
-    # value below the number of CTAs, so the combining CTAs can never see all parts.
+    # Planted arrival count -100: after every CTA arrives the counter is still below the
+    # number of CTAs, so no combining CTA ever sees all parts.
     ws[TICKETS:TICKETS + 4] = torch.tensor([0x9C, 0xFF, 0xFF, 0xFF], dtype=torch.uint8)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    _abi_decode(w, t, ws)
+    bad_out, bad_lse = _abi_decode(w, t, ws)
     torch.cuda.synchronize()
     elapsed = time.perf_counter() - t0
+    assert torch.isnan(bad_out).all() and torch.isnan(bad_lse).all()
+    # the word is sticky: until it is cleared, every call on this workspace fails closed
+    again_out, _ = _abi_decode(w, t, ws)
+    torch.cuda.synchronize()
+    assert torch.isnan(again_out).all()
     assert _status(ws) & 4
     assert elapsed < 30
     # the last combiner re-armed both counters after the timeout: the next call on the same
@@ -106,3 +113,70 @@ def test_fused_combine_wait_is_bounded_and_flagged(layer):
     torch.cuda.synchronize()
     assert _status(ws) == 0
     torch.testing.assert_close(out, ref[0], atol=1e-6, rtol=1e-6)
+
+
+def _plant_unreachable_count(device=DEV):
+    """Plants the unreachable arrival count in the current stream's ops workspace."""
+    ws = ops._workspaces.get(device, torch.cuda.current_stream(device), 1 << 20)
+    ws[TICKETS:TICKETS + 4] = torch.tensor([0x9C, 0xFF, 0xFF, 0xFF], dtype=torch.uint8,
+                                           device=device)
+    torch.cuda.synchronize()
+
+
+def test_backend_run_raises_after_a_failed_call(layer):
+    from kvssd_b200 import B200AttentionBackend, PackedBatch
+
+    w, t = layer
+    backend = B200AttentionBackend()
+    batch = PackedBatch(*t[1:], w.bits, w.group_size)
+    scale = 1.0 / math.sqrt(w.head_dim)
+    good, _ = backend.run(t[0], batch, scale)
+    backend.check(DEV)
+    good = good.clone()
+    _plant_unreachable_count()
+    bad, bad_lse = backend.run(t[0], batch, scale)  # gives up after about a second
+    torch.cuda.synchronize()
+    assert torch.isnan(bad).all() and torch.isnan(bad_lse).all()
+    with pytest.raises(ops.DeviceFailure) as info:
+        backend.run(t[0], batch, scale)  # the earlier call's failure surfaces here
+    assert info.value.status & 4
+    # raising cleared the word and re-armed the workspace: the next call is good again
+    out, _ = backend.run(t[0], batch, scale)
+    backend.check(DEV)
+    torch.testing.assert_close(out, good, atol=0, rtol=0)
+
+
+def test_pool_check_raises_after_a_failed_call(layer):
+    from kvssd_b200 import CacheSpec
+    from kvssd_b200.pool import DeviceBlockPool
+
+    w, t = layer
+    spec = CacheSpec(1, w.kv_heads, w.head_dim, w.block_tokens, w.bits, w.group_size)
+    pool = DeviceBlockPool(spec, *t[1:])
+    good, _ = pool.decode(t[0])
+    pool.check()
+    good = good.clone()
+    _plant_unreachable_count()
+    bad, _ = pool.decode(t[0])
+    with pytest.raises(ops.DeviceFailure):
+        pool.check()
+    assert torch.isnan(bad).all()
+    out, _ = pool.decode(t[0])
+    pool.check()
+    torch.testing.assert_close(out, good, atol=0, rtol=0)
+
+
+def test_out_of_pool_table_entry_raises_on_the_next_call(layer):
+    from kvssd_b200 import CacheSpec
+    from kvssd_b200.pool import DeviceBlockPool
+
+    w, t = layer
+    spec = CacheSpec(1, w.kv_heads, w.head_dim, w.block_tokens, w.bits, w.group_size)
+    pool = DeviceBlockPool(spec, *t[1:])
+    table = torch.tensor([0, 1, 10_000], dtype=torch.int32, device=DEV)
+    out, _ = pool.decode_table(t[0], table)  # the bad entry is skipped, never read
+    torch.cuda.synchronize()  # the status read of that call has landed in pinned memory
+    with pytest.raises(ops.DeviceFailure) as info:
+        pool.decode_table(t[0], table[:2].contiguous())
+    assert info.value.status & 1
+    assert torch.isfinite(out).all()

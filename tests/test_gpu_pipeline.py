@@ -140,3 +140,32 @@ def test_fused_attention_tensors_and_chunk_merge():
     mo, ml = merge_attention_chunks(halves[0][0], halves[0][1], halves[1][0], halves[1][1])
     torch.testing.assert_close(mo, out, atol=1e-5, rtol=1e-4)
     torch.testing.assert_close(ml, lse, atol=1e-5, rtol=1e-5)
+
+
+def test_pipeline_runs_a_plugged_backend(tmp_path: Path):
+    # kvssd's pipeline calls the resolved backend's run per chunk; a backend registered by the
+    # caller must be the one that runs (here a wrapper that counts its calls).
+    from kvssd_b200 import B200AttentionBackend, register_attention_backend
+
+    calls = []
+
+    class Counting(B200AttentionBackend):
+        name = "counting"
+
+        def run(self, query, batch, sm_scale):
+            calls.append(batch.packed_k.shape[0])
+            return super().run(query, batch, sm_scale)
+
+    register_attention_backend("counting", Counting)
+    store = _store(tmp_path, tokens=600)
+    q = torch.randn(32, 128, generator=torch.Generator().manual_seed(5)).half()
+    with KVSSDPipeline(store, device=DEV, stage_blocks=8, attention_backend="counting") as pipe:
+        assert isinstance(pipe.attention_backend, Counting)
+        out = pipe.decode(q.to(DEV), 0)
+    selected = store.blocks_for_layer(0)
+    assert sum(calls) == len(selected) and len(calls) == -(-len(selected) // 8)
+    ref_out, _ = _oracle_for(store, q, selected)
+    torch.testing.assert_close(out.float().cpu(), torch.from_numpy(ref_out).half().float(),
+                               atol=2e-3, rtol=1e-2)
+    with pytest.raises(ValueError, match="require_cuda_kernel conflicts"):
+        KVSSDPipeline(store, device=DEV, require_cuda_kernel=True, attention_backend="counting")

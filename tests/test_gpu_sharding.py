@@ -1,9 +1,12 @@
-"""Multi-GPU decode (needs >= 2 GPUs; skipped otherwise): the c1 configuration split over 2
-ranks, one process per GPU, against the reference backend's frozen output for the whole
-context -- token shards through the fused peer-memory exchange kernel and through NCCL, and
-KV-head shards. Also: the peer exchange under CUDA-graph replay, and a rank that skips a call
-(the other rank's kernel gives up after about a second and flags status bit 8; nothing faults
-or hangs; NVLS is off)."""
+"""Multi-GPU decode (needs >= 2 GPUs; each case is skipped when fewer GPUs than its ranks are
+visible): the c1 configuration split over 2, 4 and 8 ranks, one process per GPU, against the
+reference backend's frozen output for the whole context -- token shards through the fused
+peer-memory exchange kernel and through NCCL, and KV-head shards -- and the c2 configuration
+(1024 blocks) split over 2, 4 and 8 ranks through the peer exchange against its frozen output.
+Every call on every rank must give the same bits. Also: the peer exchange under CUDA-graph
+replay, and a rank that skips a call (the other rank's kernel gives up after about a second,
+flags status bit 8 and returns NaN; the group's collective check raises on every rank and
+re-arms the buffers; nothing faults or hangs; NVLS is off)."""
 
 from __future__ import annotations
 
@@ -28,7 +31,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _setup(rank: int, world: int, port: int):
+def _setup(rank: int, world: int, port: int, config: str = "c1"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     device = torch.device("cuda", rank)
     torch.cuda.set_device(device)
@@ -37,7 +40,7 @@ def _setup(rank: int, world: int, port: int):
     from kvssd_b200 import PackedBatch
     from kvssd_b200.workloads import WORKLOADS, make_layer
 
-    w = WORKLOADS["c1"]
+    w = WORKLOADS[config]
     layer = make_layer(w, 0, "cpu")
     batch = PackedBatch(*(t.to(device) for t in (layer.packed_k, layer.packed_v, layer.scales_k,
                                                  layer.scales_v, layer.valid_tokens)),
@@ -45,8 +48,9 @@ def _setup(rank: int, world: int, port: int):
     return device, w, batch, layer.query.to(device)
 
 
-def _rank_main(rank: int, world: int, port: int, mode: str, transport: str, results) -> None:
-    device, w, batch, q = _setup(rank, world, port)
+def _rank_main(rank: int, world: int, port: int, mode: str, transport: str, config: str,
+               results) -> None:
+    device, w, batch, q = _setup(rank, world, port, config)
     try:
         from kvssd_b200.sharding import ShardedDecoder, shard_batch_by_blocks, shard_batch_by_heads
 
@@ -66,13 +70,18 @@ def _rank_main(rank: int, world: int, port: int, mode: str, transport: str, resu
         dist.destroy_process_group()
 
 
-def _spawn(fn, *args):
+def _spawn(fn, *args, world: int = 2):
     ctx = mp.get_context("spawn")
     with ctx.Manager() as manager:
         results = manager.dict()
-        mp.start_processes(fn, args=(2, _free_port(), *args, results), nprocs=2, join=True,
-                           start_method="spawn")
+        mp.start_processes(fn, args=(world, _free_port(), *args, results), nprocs=world,
+                           join=True, start_method="spawn")
         return dict(results)
+
+
+def _needs(world: int):
+    return pytest.mark.skipif(torch.cuda.device_count() < world,
+                              reason=f"needs {world} GPUs")
 
 
 def _check(out, lse, g):
@@ -81,20 +90,29 @@ def _check(out, lse, g):
     np.testing.assert_allclose(lse, g["lse"], atol=5e-3, rtol=1e-3)
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode,transport", [("tokens", "peer"), ("tokens", "nccl"),
-                                            ("heads", "auto")])
-def test_two_gpu_sharded_decode_matches_reference(mode, transport):
-    g = load_npz("config_c1.npz")
-    results = _spawn(_rank_main, mode, transport)
-    for rank in (0, 1):
+def _check_group(results, world: int, g, transport: str) -> None:
+    for rank in range(world):
         outs, used_peer = results[rank]
         assert used_peer == (transport == "peer")
         for out, lse in outs:
             _check(out, lse, g)
-        # every call, and both ranks, give the same bits
+        # every call, and every rank, give the same bits
         assert all(np.array_equal(o, outs[0][0]) for o, _ in outs)
         assert np.array_equal(outs[0][0], results[0][0][0][0])
+
+
+@pytest.mark.parametrize("world", [pytest.param(n, marks=_needs(n)) for n in (2, 4, 8)])
+@pytest.mark.parametrize("mode,transport", [("tokens", "peer"), ("tokens", "nccl"),
+                                            ("heads", "auto")])
+def test_sharded_decode_matches_reference(mode, transport, world):
+    g = load_npz("config_c1.npz")
+    _check_group(_spawn(_rank_main, mode, transport, "c1", world=world), world, g, transport)
+
+
+@pytest.mark.parametrize("world", [pytest.param(n, marks=_needs(n)) for n in (2, 4, 8)])
+def test_sharded_c2_peer_exchange_matches_reference(world):
+    g = load_npz("config_c2.npz")
+    _check_group(_spawn(_rank_main, "tokens", "peer", "c2", world=world), world, g, "peer")
 
 
 def _graph_main(rank: int, world: int, port: int, results) -> None:
@@ -121,7 +139,7 @@ def _graph_main(rank: int, world: int, port: int, results) -> None:
         torch.cuda.synchronize(device)
         from kvssd_b200 import ops
 
-        results[rank] = (torch.equal(out, eager), ops.read_device_status(device))
+        results[rank] = (torch.equal(out, eager), ops.read_device_status_all(device))
         del g
         dec.close()
     finally:
@@ -146,19 +164,21 @@ def _skip_main(rank: int, world: int, port: int, results) -> None:
         dec = ShardedDecoder("tokens", transport="peer")
         scale = 1.0 / math.sqrt(w.head_dim)
         dec.run(q, local, scale)  # both ranks: creates the exchange, one good call
-        torch.cuda.synchronize(device)
-        ops.read_device_status(device)
-        dist.barrier()
-        if rank == 0:  # rank 1 skips this call: rank 0 must give up, not hang
-            dec.run(q, local, scale)
+        dec.check()  # collective: nothing flagged
+        nan_result = None
+        if rank == 0:  # rank 1 skips this call: rank 0 must give up, not hang, and return NaN
+            out, lse = dec.run(q, local, scale)
             torch.cuda.synchronize(device)
-        status = ops.read_device_status(device)
-        dist.barrier()
-        dec._peer.reset()  # call numbers differ now: re-zero the buffers collectively
+            nan_result = bool(torch.isnan(out).all()) and bool(torch.isnan(lse).all())
+        raised = None
+        try:
+            dec.check()  # collective: rank 0 flagged bit 8, so both ranks raise; buffers re-armed
+        except ops.DeviceFailure as exc:
+            raised = exc.status
         out, lse = dec.run(q, local, scale)
         torch.cuda.synchronize(device)
-        results[rank] = (status, ops.read_device_status(device), out.cpu().numpy(),
-                         lse.cpu().numpy())
+        results[rank] = (raised, nan_result, ops.read_device_status_all(device),
+                         out.cpu().numpy(), lse.cpu().numpy())
         dec.close()
     finally:
         dist.destroy_process_group()
@@ -168,7 +188,9 @@ def _skip_main(rank: int, world: int, port: int, results) -> None:
 def test_peer_exchange_times_out_when_a_rank_skips_a_call():
     g = load_npz("config_c1.npz")
     results = _spawn(_skip_main)
-    assert results[0][0] & 8 and results[1][0] == 0
+    assert results[0][1] is True  # the timed-out call returned NaN, not a plausible number
     for rank in (0, 1):
-        assert results[rank][1] == 0
-        _check(results[rank][2], results[rank][3], g)
+        raised, _, status, out, lse = results[rank]
+        assert raised is not None and raised & 8  # every rank learns of the failure
+        assert status == 0
+        _check(out, lse, g)  # the re-armed group decodes correctly again

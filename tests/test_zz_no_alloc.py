@@ -76,3 +76,44 @@ def test_static_scratch_rejects_geometry_beyond_its_size():
     assert "static scratch holds" in detail and str(8 << 20) in detail
     torch.cuda.synchronize()
     assert torch.count_nonzero(out) == 0
+
+
+class _DeviceBytes:
+    """A raw device address exposed to torch without a copy (CUDA array interface)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def test_static_scratch_recovers_after_a_wait_that_gave_up():
+    # A caller without an allocator cannot re-zero the scratch itself: reading the status with
+    # clear = 1 after a failed call must leave the scratch ready for the next call.
+    w = WORKLOADS["c1"]
+    layer = make_layer(w, 0, "cuda")
+    ref_out, ref_lse = ops.decode(layer.query, layer.packed_k, layer.packed_v, layer.scales_k,
+                                  layer.scales_v, layer.valid_tokens, w.bits, w.group_size,
+                                  1.0 / math.sqrt(w.head_dim))
+    scratch = ctypes.c_void_p()
+    out = torch.empty_like(ref_out)
+    lse = torch.empty_like(ref_lse)
+    _native.check(_static_decode(layer, w, out, lse, scratch), "kvssd_b200_decode_static")
+    torch.cuda.synchronize()
+    header = torch.as_tensor(_DeviceBytes(scratch.value, 2048), device="cuda")
+    # arrival count 2^32 - 100: the counter wraps below the CTA count, the combine gives up
+    header[128:132] = torch.tensor([0x9C, 0xFF, 0xFF, 0xFF], dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    _native.check(_static_decode(layer, w, out, lse, scratch), "kvssd_b200_decode_static")
+    torch.cuda.synchronize()
+    assert torch.isnan(out).all() and torch.isnan(lse).all()
+    status = ctypes.c_uint()
+    rc = _native.library().kvssd_b200_read_status(
+        scratch.value, 1, ctypes.byref(status), torch.cuda.current_stream().cuda_stream)
+    assert rc == _native.ERR_DEVICE_STATUS and status.value & 4
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(header) == 0  # status word and counters re-zeroed
+    for _ in range(2):
+        _native.check(_static_decode(layer, w, out, lse, scratch), "kvssd_b200_decode_static")
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.half(), ref_out.half(), atol=2e-3, rtol=1e-2)
+        torch.testing.assert_close(lse, ref_lse, atol=5e-3, rtol=1e-3)
