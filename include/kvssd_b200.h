@@ -87,13 +87,11 @@ KVSSD_B200_API int kvssd_b200_decode_workspace_size(int n_sel_blocks, int block_
  * (bindings.cpp:26-38, fused_decode.cu:117-121) plus the block table. Invalid block-table or
  * valid_tokens entries are never dereferenced: they are skipped/clamped and recorded in the
  * workspace status word (see kvssd_b200_read_status). Outputs: out, lse as in the header.
- * The workspace (>= kvssd_b200_decode_workspace_size bytes, 16-byte aligned) starts with an
- * 8192-byte header (KVSSD_B200_WORKSPACE_HEADER_BYTES) holding that sticky status word and the
- * state of the fused combine (the streaming kernel folds its split-KV parts itself): two
- * counters that return to their starting values after every call, a generation word that
- * moves on by one per call and per-part ready flags tagged with it. Zero the header once
- * after allocating the workspace. Calls sharing one workspace must be ordered on the GPU (same
- * stream or explicit events). */
+ * The workspace (>= kvssd_b200_decode_workspace_size bytes, 16-byte aligned) starts with a
+ * 2048-byte header holding that sticky status word and the counters of the fused combine
+ * (the streaming kernel folds its split-KV parts itself; the counters return to zero at the
+ * end of every call): zero the header once after allocating the workspace. Calls
+ * sharing one workspace must be ordered on the GPU (same stream or explicit events). */
 KVSSD_B200_API int kvssd_b200_decode(const void* query, int query_dtype, const uint8_t* packed_k,
                       const uint8_t* packed_v, const uint16_t* scales_k,
                       const uint16_t* scales_v, const int32_t* valid_tokens,
@@ -101,9 +99,6 @@ KVSSD_B200_API int kvssd_b200_decode(const void* query, int query_dtype, const u
                       int block_tokens, int query_heads, int kv_heads, int head_dim, int bits,
                       int group_size, float sm_scale, float* out, float* lse, void* workspace,
                       size_t workspace_bytes, kvssd_b200_stream_t stream);
-
-/* Bytes at the start of a decode workspace that must be zero before its first use. */
-#define KVSSD_B200_WORKSPACE_HEADER_BYTES 8192u
 
 /* Bytes of the device scratch behind kvssd_b200_decode_static (one array per device). */
 #define KVSSD_B200_STATIC_SCRATCH_BYTES (8u << 20)
@@ -115,10 +110,10 @@ KVSSD_B200_API int kvssd_b200_decode(const void* query, int query_dtype, const u
  * For callers that cannot allocate device memory on the decode path: hosts that bind the C ABI
  * without a device allocator of their own (a plain C, cgo or JNI host), and serving loops
  * that must not call cudaMalloc/cudaFree there, which synchronise the device.
- * Limits: a geometry whose plan needs more than KVSSD_B200_STATIC_SCRATCH_BYTES (8192 bytes of
+ * Limits: a geometry whose plan needs more than KVSSD_B200_STATIC_SCRATCH_BYTES (2048 bytes of
  * header plus n_parts * query_heads * (head_dim + 2) * 4; the c2 shape needs 2.5 MB) is
  * rejected with KVSSD_B200_ERR_WORKSPACE before anything is launched. The first call on each
- * device resolves the scratch address and zeroes its 8192-byte header (the only part
+ * device resolves the scratch address and zeroes its 2048-byte header (the only part
  * that must start at zero) on `stream`; make that first call before any stream capture.
  * The address is kept per device and driver context: after cudaDeviceReset the next call
  * (again before any capture) sets the new context's scratch up the same way. After a call
@@ -228,7 +223,7 @@ KVSSD_B200_API int kvssd_b200_decode_batched_workspace_size(int n_problems, int 
  * descriptor contents). The grid gets floor(SMs / n_problems) CTAs per problem (at least 1);
  * each problem's split-KV parts are folded by its own CTAs in the grid's tail. Needs the
  * streaming kernel's shapes (INT4, head_dim 128, group 32 or 64, 16-byte aligned operands)
- * and n_problems <= the SM count; workspace as kvssd_b200_decode (zero its 8192-byte header
+ * and n_problems <= the SM count; workspace as kvssd_b200_decode (zero its 2048-byte header
  * once). Amortises the per-decode tail and launch over a multi-layer step or a batch of
  * sequences (the reference decodes one layer per call, src/kvssd/pipeline.py:167-187). No
  * reference counterpart. */
@@ -291,7 +286,7 @@ KVSSD_B200_API int kvssd_b200_decode_exchange(const void* query, int query_dtype
  * up waiting for its copies). After bits 4, 8 or 32 the kernels write NaN into out and lse of
  * that call and of every later call on the workspace until the word is cleared, so a failure
  * is never returned as a plausible number. clear = 1 with a nonzero word re-zeroes the
- * workspace's whole 8192-byte header (status word, counters, generation and ready flags), which makes the
+ * workspace's whole 2048-byte header (status word and arrival counters), which makes the
  * workspace usable again. Returns KVSSD_B200_ERR_DEVICE_STATUS when the word is nonzero. No
  * reference counterpart (the reference raises through TORCH_CHECK,
  * csrc/fused_decode.cu:141). */

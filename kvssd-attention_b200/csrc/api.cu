@@ -58,19 +58,12 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(KVSSD_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-// Workspace header, zeroed once by the caller: the device status word (byte 0), the fused
-// combine's generation word (byte 64; the tag of the next call's part-ready flags is its value
-// + 1) and flag-withholding test word (byte 68, zero in normal use), the fused combine's
-// arrival and combiner counters (byte 128), the batched decode's pair per problem (byte 256,
-// up to 148 problems) and the per-part ready flags of a single decode (byte 4096, up to 1024
-// parts). The counters are back at their starting values after every call; the generation
-// moves on by one per call.
-constexpr size_t kHeaderBytes = 8192;
-constexpr size_t kGenOffset = 64;
+// Workspace header, zeroed once by the caller and zero again after every call: the device
+// status word (byte 0), the fused combine's arrival and combiner counters (byte 128) and the
+// batched decode's pair per problem (byte 256, up to 148 problems).
+constexpr size_t kHeaderBytes = 2048;
 constexpr size_t kTicketOffset = 128;
 constexpr size_t kProblemTicketOffset = 256;
-constexpr size_t kFlagsOffset = 4096;
-constexpr int kMaxFlagParts = static_cast<int>((kHeaderBytes - kFlagsOffset) / sizeof(unsigned));
 constexpr int kMaxParts = 8192;       // bound on split-KV parts
 
 struct DeviceInfo {
@@ -233,7 +226,6 @@ int make_plan(const Geometry& g, bool aligned, bool allow_stream, Plan& p,
   }
   const int parts_per_split = p.streaming ? 1 : p.wph;  // merged in-CTA by the streaming kernel
   splits = std::min<long long>(splits, kMaxParts / parts_per_split);
-  if (p.streaming) splits = std::min<long long>(splits, kMaxFlagParts);  // one ready flag each
   p.n_splits = static_cast<int>(splits);
   p.n_parts = p.n_splits * parts_per_split;
   const size_t part_floats = static_cast<size_t>(p.n_parts) * g.qh * (g.d + 2);
@@ -392,8 +384,6 @@ int prepare_decode(const void* query, int query_dtype, const uint8_t* packed_k,
   char* ws = static_cast<char*>(workspace);
   a.status = reinterpret_cast<unsigned*>(ws);
   a.tickets = reinterpret_cast<unsigned*>(ws + kTicketOffset);
-  a.flags = reinterpret_cast<unsigned*>(ws + kFlagsOffset);
-  a.gen = reinterpret_cast<unsigned*>(ws + kGenOffset);
   a.fuse_combine = 0;
   a.out = nullptr;
   a.lse = nullptr;
@@ -862,7 +852,7 @@ int plan_batched(int n_problems, int block_tokens, int query_heads, int kv_heads
   bp.ctas = std::max(1, info.sms / n_problems);
   p.n_splits = bp.ctas;
   p.n_parts = bp.ctas * n_problems;
-  if (kProblemTicketOffset + static_cast<size_t>(2) * n_problems * sizeof(unsigned) > kFlagsOffset)
+  if (kProblemTicketOffset + static_cast<size_t>(2) * n_problems * sizeof(unsigned) > kHeaderBytes)
     return fail(KVSSD_B200_ERR_UNSUPPORTED, "too many problems for the workspace header");
   bp.ws_bytes = kHeaderBytes +
                 static_cast<size_t>(p.n_parts) * query_heads * (head_dim + 2) * sizeof(float);
@@ -923,8 +913,6 @@ int kvssd_b200_decode_batched(const kvssd_b200_problem* problems, int n_problems
   char* ws = static_cast<char*>(workspace);
   a.status = reinterpret_cast<unsigned*>(ws);
   a.problem_tickets = reinterpret_cast<unsigned*>(ws + kProblemTicketOffset);
-  a.flags = nullptr;  // problems count their arrivals (problem_tickets)
-  a.gen = reinterpret_cast<unsigned*>(ws + kGenOffset);
   a.part_ml = reinterpret_cast<float*>(ws + kHeaderBytes);
   a.part_acc = a.part_ml + static_cast<size_t>(p.n_parts) * query_heads * 2;
   a.problems = problems;

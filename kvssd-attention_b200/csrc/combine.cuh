@@ -98,101 +98,6 @@ __device__ __forceinline__ void combine_slice_result(const float* __restrict__ p
   __syncthreads();  // the shared arrays may be reused by the caller's next slice
 }
 
-// combine_slice_result for parts that may still be in flight: before a warp loads a batch of
-// parts, the lane of each part waits (bounded) until the part's ready flag holds `tag` (the
-// writing CTA stores it with release semantics after its part). So the parts that are already
-// complete are folded while other CTAs still stream, and only the last parts' round trip
-// remains after the final one lands. *timed_out (every thread of the block) is true when some
-// wait gave up (the missing parts are then left out of the fold).
-__device__ __forceinline__ void combine_slice_result_flags(
-    const float* __restrict__ part_acc, const float* __restrict__ part_ml,
-    const unsigned* __restrict__ flags, unsigned tag, int n_parts, int qh, int d, int h,
-    int chunk, unsigned long long wait_ns, unsigned max_polls, float* o, float* l2,
-    bool* timed_out) {
-  __shared__ float wm[kCombineWarps], wl[kCombineWarps], wacc[kCombineWarps][32];
-  __shared__ int any_timeout;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int dd = chunk * 32 + lane;
-  const bool has_dim = dd < d;
-  const bool active = warp < kCombineWarps;
-  const int lo = active ? static_cast<int>(static_cast<long long>(n_parts) * warp / kCombineWarps) : 0;
-  const int hi = active ? static_cast<int>(static_cast<long long>(n_parts) * (warp + 1) / kCombineWarps) : 0;
-  const size_t stride = static_cast<size_t>(qh) * d;
-  if (threadIdx.x == 0) any_timeout = 0;
-  __syncthreads();
-  float M = -INFINITY, L = 0.f, A = 0.f;
-  bool gave_up = false;
-  for (int base = lo; base < hi; base += 32) {
-    const int p = base + lane;
-    bool ready = p >= hi;
-    const unsigned long long t0 = global_ns();
-    unsigned polls = 0;
-    while (!__all_sync(0xffffffffu, ready)) {
-      if (!ready) ready = ld_acquire_gpu(flags + p) == tag;
-      const bool expired = ++polls > max_polls || global_ns() - t0 > wait_ns;
-      if (__shfl_sync(0xffffffffu, expired, 0)) {
-        gave_up = true;
-        break;
-      }
-    }
-    __syncwarp();  // the lanes' acquires order every lane's loads of the batch below
-    float mp = -INFINITY, lp = 0.f;
-    if (p < hi && ready) {
-      const float2 ml =
-          __ldcg(reinterpret_cast<const float2*>(part_ml + (static_cast<size_t>(p) * qh + h) * 2));
-      mp = ml.x;
-      lp = ml.y;
-    }
-    const unsigned have = __ballot_sync(0xffffffffu, p < hi && ready);
-    const float* row = part_acc + (static_cast<size_t>(base) * qh + h) * d + dd;
-    float v[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      v[j] = (((have >> j) & 1u) && has_dim) ? __ldcg(row + j * stride) : 0.f;
-    float cm = mp;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, off));
-    const float nm = fmaxf(M, cm);
-    if (nm == -INFINITY) continue;
-    const float keep = fast_exp2(M - nm);
-    const float wp = mp == -INFINITY ? 0.f : fast_exp2(mp - nm);
-    float ls = wp * lp;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
-    L = fmaf(L, keep, ls);
-    A *= keep;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) A = fmaf(__shfl_sync(0xffffffffu, wp, j), v[j], A);
-    M = nm;
-  }
-  if (active) {
-    if (lane == 0) {
-      wm[warp] = M;
-      wl[warp] = L;
-      if (gave_up) any_timeout = 1;
-    }
-    wacc[warp][lane] = A;
-  }
-  __syncthreads();
-  *timed_out = any_timeout != 0;
-  if (warp == 0) {
-    float mx = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kCombineWarps; ++w) mx = fmaxf(mx, wm[w]);
-    float ls = 0.f, t = 0.f;
-#pragma unroll
-    for (int w = 0; w < kCombineWarps; ++w) {
-      const float ww = wm[w] == -INFINITY ? 0.f : fast_exp2(wm[w] - mx);
-      ls = fmaf(ww, wl[w], ls);
-      t = fmaf(ww, wacc[w][lane], t);
-    }
-    const bool empty = (mx == -INFINITY) || !(ls > 0.f);
-    *o = empty ? 0.f : t / ls;
-    *l2 = empty ? -INFINITY : mx + log2f(ls);
-  }
-  __syncthreads();
-}
-
 // The slice's normalised output and natural-log LSE written to out [qh, d] / lse [qh].
 // poison: write NaN instead (see kDevFatalBits).
 __device__ __forceinline__ void combine_slice(const float* __restrict__ part_acc,

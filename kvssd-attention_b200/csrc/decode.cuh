@@ -46,11 +46,6 @@ struct DecodeArgs {
   // Fused combine (streaming kernel): the last CTAs to finish fold all parts into out/lse.
   int fuse_combine;
   unsigned* tickets;  // [0] CTAs that wrote their part, [1] combiners done; zero between calls
-  // Part-ready flags of a single decode's fused combine (nullptr: the batched decode, which
-  // counts arrivals instead): CTA x stores the call's tag in flags[x] once its part is
-  // written; the tag is the generation word + 1, and the generation moves on every call.
-  unsigned* flags;
-  unsigned* gen;
   float* out;         // [qh, d] normalised output
   float* lse;         // [qh] natural-log LSE
   // Cross-GPU exchange (token-range shards, fused combine only): every combiner pushes its

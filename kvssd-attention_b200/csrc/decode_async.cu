@@ -115,7 +115,6 @@ __device__ __forceinline__ void async_decode_body(const DecodeArgs& a) {
   // Exchange epoch of this call (completed calls + 1), read before this CTA's arrival.
   const unsigned epoch =
       a.xworld ? *reinterpret_cast<const volatile unsigned*>(a.xpeers[a.xrank]) + 1u : 0u;
-  const unsigned tag = part_tag(a);  // this call's part-ready flag value
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, c = lane & 3;
   const int h = warp % KVH, sub = warp / KVH;
@@ -221,7 +220,7 @@ __device__ __forceinline__ void async_decode_body(const DecodeArgs& a) {
   cp_async_wait<0>();
   __syncthreads();
   merge_warps_write_part<KVH>(a, reinterpret_cast<float*>(smem), warp, lane, q0, nq, state);
-  if (a.fuse_combine) fused_combine_tail<D>(a, epoch, tag, a.n_splits);
+  if (a.fuse_combine) fused_combine_tail<D>(a, epoch, a.n_splits);
 }
 
 template <int KVH, int GROUP>

@@ -90,90 +90,25 @@ __device__ __forceinline__ void exchange_slice(const DecodeArgs& a, unsigned epo
     a.lse[h] = bad ? nan_f32() : empty ? -INFINITY : (M + log2f(den)) * kLn2;
 }
 
-// The tag of this call's part-ready flags (0 without flags): read by every CTA after
-// griddepcontrol.wait, so the previous call on the workspace has finished moving it on.
-__device__ __forceinline__ unsigned part_tag(const DecodeArgs& a) {
-  return a.flags ? *reinterpret_cast<const volatile unsigned*>(a.gen) + 1u : 0u;
-}
-
 // Fused split-KV combine at the end of the decode grid (launched cooperatively, so all CTAs
-// are co-resident).
-//
-// Single decode (a.flags set): every CTA takes an arrival number from tickets[0], then
-// publishes its part by storing the call's tag in its flag (release). The first n_comb CTAs to
-// arrive (one per (query head, 32-dim) slice, or fewer when the grid is smaller) fold one or
-// more slices each, waiting part by part (combine_slice_result_flags), so the parts already
-// written are folded while the last CTAs still stream, and the CTAs that finish last are not
-// the ones that fold. Both counters count with atomicInc, which wraps them back to zero after
-// the call's n_splits arrivals and n_comb combiners (a counter that starts anywhere below its
-// bound still hands out every number once). The last combiner to finish moves the generation
-// on (the next call's tag) and publishes the exchange epoch. Header word gen[1] names a CTA
-// (index + 1) that withholds its flag: 0 in normal use; tests set it to make the combine's
-// bounded wait run out with nothing faulting.
-//
-// Batched decode (a.flags null): every CTA signals its arrival with one release add on
-// tickets[0]; the n_comb highest-numbered CTAs of the problem wait until all n_splits parts
-// have arrived and fold their slices; each combiner counts itself on tickets[1] as soon as it
-// has seen every arrival, and the last one re-arms both counters after its fold.
-//
-// Every wait is bounded: on timeout the CTA flags kDevCombineTimeout and carries on. A combiner
-// that timed out, or that finds a fatal bit in the status word once it has every part
+// are co-resident). Every CTA publishes its part and signals its arrival with one release add
+// on tickets[0]; the n_comb highest-numbered CTAs (one per (query head, 32-dim) slice, or
+// fewer when the grid is smaller) wait until all n_splits parts have arrived and fold one or
+// more slices each. Each combiner counts itself on tickets[1] as soon as it has seen every
+// arrival -- the atomic's round trip overlaps its fold -- and the last one re-arms both
+// counters (zero again for the next call) and publishes the exchange epoch after its fold.
+// The wait is bounded: on timeout the CTA flags kDevCombineTimeout and carries on. A combiner
+// that timed out, or that finds a fatal bit in the status word once every part has arrived
 // (another CTA gave up on its copies, or an earlier call on this workspace failed and nobody
 // has cleared the word), writes NaN into its slices of out and lse.
 template <int D>
 __device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned epoch,
-                                                   unsigned tag, int n_parts) {
-  __shared__ int poison_flag, arrival;
+                                                   int n_parts) {
+  __shared__ int poison_flag;
   __syncthreads();  // every warp's part stores precede the CTA's release below
   constexpr int kChunks = (D + 31) / 32;
   const int n_slices = a.qh * kChunks;
   const int n_comb = min(a.n_splits, n_slices);
-  if (a.flags) {
-    if (threadIdx.x == 0) {
-      arrival = static_cast<int>(atomicInc(a.tickets, static_cast<unsigned>(a.n_splits) - 1u));
-      const unsigned withhold = reinterpret_cast<const volatile unsigned*>(a.gen)[1];
-      if (withhold != blockIdx.x + 1u)
-        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.flags + blockIdx.x), "r"(tag)
-                     : "memory");
-    }
-    __syncthreads();
-    const unsigned k = static_cast<unsigned>(arrival);
-    if (k >= static_cast<unsigned>(n_comb)) return;
-    bool any_timeout = false;
-    for (int sl = static_cast<int>(k); sl < n_slices; sl += n_comb) {
-      float o = 0.f, l2 = -INFINITY;
-      bool timed_out = false;
-      combine_slice_result_flags(a.part_acc, a.part_ml, a.flags, tag, n_parts, a.qh, D,
-                                 sl / kChunks, sl % kChunks, kCombineWaitNs, kCombineMaxPolls,
-                                 &o, &l2, &timed_out);
-      any_timeout = any_timeout || timed_out;
-      // every part of the slice is in (or given up on): decide whether the result is usable
-      if (threadIdx.x == 0) {
-        if (timed_out) atomicOr(a.status, kDevCombineTimeout);
-        poison_flag = any_timeout || (ld_acquire_gpu(a.status) & kDevFatalBits) != 0u;
-      }
-      __syncthreads();
-      const bool poison = poison_flag != 0;
-      if (threadIdx.x < 32) {
-        if (a.xworld == 0) {
-          const int lane = threadIdx.x, h = sl / kChunks, chunk = sl % kChunks;
-          const int dd = chunk * 32 + lane;
-          if (dd < D) a.out[static_cast<size_t>(h) * D + dd] = poison ? nan_f32() : o;
-          if (chunk == 0 && lane == 0) a.lse[h] = poison ? nan_f32() : l2 * kLn2;
-        } else {
-          exchange_slice<D>(a, epoch, sl, n_slices, o, l2, poison);
-        }
-      }
-      __syncthreads();
-    }
-    const unsigned last = static_cast<unsigned>(n_comb) - 1u;
-    if (threadIdx.x == 0 && atomicInc(a.tickets + 1, last) == last) {
-      // Every combiner has folded every part: the generation moves on for the next call.
-      atomicExch(a.gen, tag);
-      if (a.xworld) *reinterpret_cast<volatile unsigned*>(a.xpeers[a.xrank]) = epoch;
-    }
-    return;
-  }
   const int k = static_cast<int>(blockIdx.x) - (a.n_splits - n_comb);
   if (threadIdx.x == 0) {
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.tickets) : "memory");
@@ -214,13 +149,23 @@ __device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned
     }
     __syncthreads();
   } else {
-    for (int sl = k; sl < n_slices; sl += n_comb)
+  for (int sl = k; sl < n_slices; sl += n_comb) {
+    if (a.xworld == 0) {
       combine_slice(a.part_acc, a.part_ml, n_parts, a.qh, D, sl / kChunks, sl % kChunks,
                     a.out, a.lse, poison);
+    } else {
+      float o = 0.f, l2 = -INFINITY;
+      combine_slice_result(a.part_acc, a.part_ml, n_parts, a.qh, D, sl / kChunks,
+                           sl % kChunks, &o, &l2);
+      if (threadIdx.x < 32) exchange_slice<D>(a, epoch, sl, n_slices, o, l2, poison);
+    }
+  }
   }
   if (threadIdx.x == 0 && combined_before == static_cast<unsigned>(n_comb) - 1) {
     atomicExch(a.tickets, 0u);
     atomicExch(a.tickets + 1, 0u);
+    // every CTA read the epoch at its start, before its arrival: publish the completed call
+    if (a.xworld) *reinterpret_cast<volatile unsigned*>(a.xpeers[a.xrank]) = epoch;
   }
 }
 

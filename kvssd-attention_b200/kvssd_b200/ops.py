@@ -22,7 +22,7 @@ _QUERY_DTYPES = {
     torch.float64: _native.Q_F64,
 }
 
-_WORKSPACE_HEADER = 8192  # the workspace header that starts at zero (include/kvssd_b200.h)
+_WORKSPACE_HEADER = 2048
 
 
 class _Workspaces:

@@ -1,10 +1,9 @@
 """The streaming kernel's fused split-KV combine: equality with the two-launch path, the
-arrival counters returning to zero, and the bounded wait (the header's flag-withholding word
-makes one CTA keep its part-ready flag back -- a flag that nothing sets -- so the combining CTAs
-give up after about a second and flag status bit 4; nothing faults or hangs). A call that gave
-up returns NaN, later calls on the workspace return NaN until the status word is cleared, and
-the public entry points (the ``cuda`` backend's run, DeviceBlockPool) raise ops.DeviceFailure
-on the next call instead of returning a number."""
+arrival counters returning to zero, and the bounded wait (a planted counter value that can
+never be reached makes the combining CTAs give up after about a second and flag status bit 4;
+nothing faults or hangs). A call that gave up returns NaN, later calls on the workspace return
+NaN until the status word is cleared, and the public entry points (the ``cuda`` backend's run,
+DeviceBlockPool) raise ops.DeviceFailure on the next call instead of returning a number."""
 
 from __future__ import annotations
 
@@ -20,7 +19,6 @@ from kvssd_b200.workloads import WORKLOADS, make_layer
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 TICKETS = 128  # byte offset of the two combine counters in the workspace header
-WITHHOLD = 68  # header word: index + 1 of a CTA that keeps its part-ready flag back
 
 
 @pytest.fixture(scope="module")
@@ -91,8 +89,9 @@ def test_fused_combine_equals_two_launch_combine_and_resets_counters(layer):
 def test_fused_combine_wait_is_bounded_and_flagged(layer):
     w, t = layer
     ws = _workspace(w, t)
-    # CTA 0 keeps its ready flag back: every combining CTA waits for that part and gives up.
-    ws[WITHHOLD:WITHHOLD + 4] = torch.tensor([1, 0, 0, 0], dtype=torch.uint8)
+    # Planted arrival count -100: after every CTA arrives the counter is still below the
+    # number of CTAs, so no combining CTA ever sees all parts.
+    ws[TICKETS:TICKETS + 4] = torch.tensor([0x9C, 0xFF, 0xFF, 0xFF], dtype=torch.uint8)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     bad_out, bad_lse = _abi_decode(w, t, ws)
@@ -105,9 +104,10 @@ def test_fused_combine_wait_is_bounded_and_flagged(layer):
     assert torch.isnan(again_out).all()
     assert _status(ws) & 4
     assert elapsed < 30
-    # reading the status with clear = 1 re-zeroed the header (status word, counters and the
-    # withholding word): the next call on the same workspace is correct
-    assert torch.count_nonzero(ws[:8192]) == 0
+    # the last combiner re-armed both counters after the timeout: the next call on the same
+    # workspace is correct without the caller touching them
+    assert torch.count_nonzero(ws[TICKETS:TICKETS + 8]) == 0
+    ws[:4].zero_()  # the sticky status word is the caller's to clear
     out, lse = _abi_decode(w, t, ws)
     ref = ops.decode(*t, w.bits, w.group_size, 1.0 / math.sqrt(w.head_dim))
     torch.cuda.synchronize()
@@ -115,11 +115,11 @@ def test_fused_combine_wait_is_bounded_and_flagged(layer):
     torch.testing.assert_close(out, ref[0], atol=1e-6, rtol=1e-6)
 
 
-def _withhold_one_flag(device=DEV):
-    """Makes CTA 0 of the next decode on the current stream's ops workspace keep its ready
-    flag back (the combine's wait then runs out)."""
+def _plant_unreachable_count(device=DEV):
+    """Plants the unreachable arrival count in the current stream's ops workspace."""
     ws = ops._workspaces.get(device, torch.cuda.current_stream(device), 1 << 20)
-    ws[WITHHOLD:WITHHOLD + 4] = torch.tensor([1, 0, 0, 0], dtype=torch.uint8, device=device)
+    ws[TICKETS:TICKETS + 4] = torch.tensor([0x9C, 0xFF, 0xFF, 0xFF], dtype=torch.uint8,
+                                           device=device)
     torch.cuda.synchronize()
 
 
@@ -133,7 +133,7 @@ def test_backend_run_raises_after_a_failed_call(layer):
     good, _ = backend.run(t[0], batch, scale)
     backend.check(DEV)
     good = good.clone()
-    _withhold_one_flag()
+    _plant_unreachable_count()
     bad, bad_lse = backend.run(t[0], batch, scale)  # gives up after about a second
     torch.cuda.synchronize()
     assert torch.isnan(bad).all() and torch.isnan(bad_lse).all()
@@ -156,7 +156,7 @@ def test_pool_check_raises_after_a_failed_call(layer):
     good, _ = pool.decode(t[0])
     pool.check()
     good = good.clone()
-    _withhold_one_flag()
+    _plant_unreachable_count()
     bad, _ = pool.decode(t[0])
     with pytest.raises(ops.DeviceFailure):
         pool.check()

@@ -99,9 +99,9 @@ def test_static_scratch_recovers_after_a_wait_that_gave_up():
     lse = torch.empty_like(ref_lse)
     _native.check(_static_decode(layer, w, out, lse, scratch), "kvssd_b200_decode_static")
     torch.cuda.synchronize()
-    header = torch.as_tensor(_DeviceBytes(scratch.value, 8192), device="cuda")
-    # header word 68 = 1: CTA 0 keeps its part-ready flag back, so the combine's wait runs out
-    header[68:72] = torch.tensor([1, 0, 0, 0], dtype=torch.uint8, device="cuda")
+    header = torch.as_tensor(_DeviceBytes(scratch.value, 2048), device="cuda")
+    # arrival count 2^32 - 100: the counter wraps below the CTA count, the combine gives up
+    header[128:132] = torch.tensor([0x9C, 0xFF, 0xFF, 0xFF], dtype=torch.uint8, device="cuda")
     torch.cuda.synchronize()
     _native.check(_static_decode(layer, w, out, lse, scratch), "kvssd_b200_decode_static")
     torch.cuda.synchronize()
@@ -111,7 +111,7 @@ def test_static_scratch_recovers_after_a_wait_that_gave_up():
         scratch.value, 1, ctypes.byref(status), torch.cuda.current_stream().cuda_stream)
     assert rc == _native.ERR_DEVICE_STATUS and status.value & 4
     torch.cuda.synchronize()
-    assert torch.count_nonzero(header) == 0  # status word, counters and flags re-zeroed
+    assert torch.count_nonzero(header) == 0  # status word and counters re-zeroed
     for _ in range(2):
         _native.check(_static_decode(layer, w, out, lse, scratch), "kvssd_b200_decode_static")
         torch.cuda.synchronize()
