@@ -18,9 +18,10 @@
 //
 // Synchronisation: per stage a "full" mbarrier (the producer's arrive with the stage's byte
 // count; the TMA completes the bytes) and an "empty" mbarrier (one arrive per consumer warp of
-// the group, after its QK MMAs have consumed the tile's last shared-memory loads). Each
-// consumer group has its own producer warp (warp 16 + group), which blocks on its ring's next
-// empty barrier: no group waits behind another, and a waiting producer takes no issue slots.
+// the group, after its QK MMAs have consumed the tile's last shared-memory loads). Four
+// producer warps (16-19, one per SM sub-partition) fill the rings: group g's stages are split
+// among producers g, g + WPH, ... by stage index; a producer blocks on the next empty barrier
+// of its own stages, so no group waits behind another.
 // Every wait is bounded (about a second, and a poll count): on timeout the kernel flags
 // kDevStreamTimeout, waits (bounded) for the copies it issued, and finishes with what it has.
 #include <cuda.h>
@@ -41,10 +42,17 @@ struct TmaMaps {
 constexpr int kTmaSlots = 4;  // ring stages per consumer group
 constexpr uint32_t kTmaMaxPolls = 1u << 26;
 
+// Producer warps: four, one per SM sub-partition (warp w runs on sub-partition w % 4). A
+// sub-partition that hosts a producer warp runs its consumer warps measurably slower (the CTA
+// then waits ~2 us for them at its end), so every sub-partition gets exactly one producer and
+// the consumer groups share them: group g's stages are issued by producers g, g + WPH, ...
+constexpr int kTmaProducers = 4;
+
 template <int KVH, int G, int BITS>
 struct TmaLayout {
-  static constexpr int WPH = kStreamWarps / KVH;  // consumer groups = producer warps
-  static constexpr int THREADS = 32 * (kStreamWarps + WPH);
+  static constexpr int WPH = kStreamWarps / KVH;  // consumer groups (each with its own ring)
+  static constexpr int PPG = kTmaProducers / WPH;  // producer warps per group
+  static constexpr int THREADS = 32 * (kStreamWarps + kTmaProducers);
   static constexpr int NS = WPH * kTmaSlots;      // ring stages
   static constexpr int PD = 16 * BITS;            // code bytes per (token, head): 64 or 32
   static constexpr int HEAD_TILE = 16 * PD;       // one head's 16 rows in a stage
@@ -114,26 +122,30 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP, BITS>::THREADS, 1)
 
   const long long t_begin = a.total_tiles * blockIdx.x / a.n_splits;
   const int n_tiles = static_cast<int>(a.total_tiles * (blockIdx.x + 1) / a.n_splits - t_begin);
-  int issued = 0;  // producer: stages issued to its group
+  int issued = 0;  // producer: the group's stages up to and including its last own one
   StreamState state;
   const int q0 = h * a.gqa, nq = a.gqa;
 
+  // Producer pi serves consumer group gp = pi % WPH and issues the group's stages i with
+  // i % PPG == pp (pp = pi / WPH); `issued` counts the group's stages up to its last own one.
+  const int pi = warp - kStreamWarps, gp = pi % L::WPH, pp = pi / L::WPH;
   if (warp >= kStreamWarps) {
-    // ---------------- producer of group gp
-    const int gp = warp - kStreamWarps;
+    // ---------------- producer pp of group gp
     const uint64_t policy = l2_evict_first();
     BlockInfoCache cache;
+    const int n_group = gp < n_tiles ? (n_tiles - gp + L::WPH - 1) / L::WPH : 0;
 #pragma unroll 1
-    for (int k = gp; k < n_tiles; k += L::WPH, ++issued) {
-      const int sl = gp * kTmaSlots + issued % kTmaSlots;
+    for (int i = pp; i < n_group; i += L::PPG) {
+      const int sl = gp * kTmaSlots + i % kTmaSlots;
       const bool free_slot = mbar_wait_until(smem_addr(&empty[sl]),
-                                             ((issued / kTmaSlots) & 1) ^ 1, deadline,
+                                             ((i / kTmaSlots) & 1) ^ 1, deadline,
                                              kTmaMaxPolls);
       if (!__all_sync(0xffffffffu, free_slot)) {  // the warp leaves together
         if (lane == 0) atomicOr(a.status, kDevStreamTimeout);
         break;
       }
-      const long long t = t_begin + k;
+      issued = i + 1;
+      const long long t = t_begin + gp + static_cast<long long>(i) * L::WPH;
       const int slot = static_cast<int>(t / a.tiles_per_block);
       const int tib = static_cast<int>(t - static_cast<long long>(slot) * a.tiles_per_block);
       const uint32_t bar = smem_addr(&full[sl]);
@@ -244,14 +256,15 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP, BITS>::THREADS, 1)
   }
   __syncthreads();
   if (warp >= kStreamWarps && lane == 0) {
-    // Copies still in flight can only be the group's last kTmaSlots stages (after a timeout)
-    // and the query copy; wait for them (bounded) before the ring is reused and the CTA exits.
-    const int gp = warp - kStreamWarps;
+    // Copies still in flight can only be this producer's stages among the group's last
+    // kTmaSlots (after a timeout) and the query copy; wait for them (bounded) before the ring
+    // is reused and the CTA exits.
     const unsigned long long drain_deadline = global_ns() + kCombineWaitNs;
-    if (gp == 0 && q_staged && !mbar_wait_until(smem_addr(&q_bar), 0, drain_deadline, kTmaMaxPolls))
+    if (pi == 0 && q_staged && !mbar_wait_until(smem_addr(&q_bar), 0, drain_deadline, kTmaMaxPolls))
       atomicOr(a.status, kDevStreamTimeout);
     for (int idx = max(0, issued - kTmaSlots); idx < issued; ++idx)
-      if (!mbar_wait_until(smem_addr(&full[gp * kTmaSlots + idx % kTmaSlots]),
+      if (idx % L::PPG == pp &&
+          !mbar_wait_until(smem_addr(&full[gp * kTmaSlots + idx % kTmaSlots]),
                            (idx / kTmaSlots) & 1, drain_deadline, kTmaMaxPolls))
         atomicOr(a.status, kDevStreamTimeout);
   }
@@ -409,7 +422,7 @@ size_t tma_decode_smem(int kvh, int group, int bits) {
 }
 
 int tma_decode_threads(int kvh, int group) {
-  // the thread count depends on the KV heads only (16 consumers + one producer per group)
+  // the thread count is the same for every geometry: 16 consumers + 4 producers
   return group == 32 ? tma_threads_for_heads<4, 4>(kvh) : tma_threads_for_heads<2, 4>(kvh);
 }
 
