@@ -804,7 +804,10 @@ int kvssd_b200_decode_records(const uint8_t* records, size_t record_stride, int 
   a.scales_v = reinterpret_cast<uint8_t*>(scales_v);
   a.valid = valid_tokens;
   a.status = record_status;
-  cudaError_t e = launch_record_decode(a, reinterpret_cast<cudaStream_t>(stream));
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "record decode device");
+  e = launch_record_decode(a, device_info(dev).sms, reinterpret_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? KVSSD_B200_OK : cuda_fail(e, "record decode launch");
 }
 

@@ -110,3 +110,67 @@ def test_pool_from_store_checks_crc_on_device(tmp_path):
     with pytest.raises(IOError, match="CRC mismatch"):
         DeviceBlockPool.from_store(store, 0, DEV)
     DeviceBlockPool.from_store(store, 0, DEV, verify_crc=False)
+
+
+def _encoded(spec, n, seed):
+    gen = torch.Generator().manual_seed(seed)
+    shape = (spec.block_tokens, spec.kv_heads, spec.head_dim)
+    records = []
+    for b in range(n):
+        x = torch.randn(2, *shape, generator=gen).half()
+        kq = quantize_tensor(x[0], spec.bits, spec.group_size)
+        vq = quantize_tensor(x[1], spec.bits, spec.group_size)
+        rec, _ = encode_record(PackedKVBlock(0, b, spec.block_tokens - b % 5, kq, vq), spec)
+        records.append(torch.frombuffer(bytearray(rec), dtype=torch.uint8))
+    return torch.stack(records)
+
+
+@pytest.mark.parametrize("n", [1, 2, 37])
+def test_streaming_decode_runs_across_records(n):
+    """The c2 record geometry (289 rows of 512 bytes per record, 3 rows per chunk): one record
+    is split over many warps, 37 records give runs that end mid-record and cross records."""
+    spec = CacheSpec(layers=1, kv_heads=8, head_dim=128, block_tokens=128, bits=4, group_size=32)
+    raw = _encoded(spec, n, 100 + n)
+    out = ops.decode_records(raw.to(DEV), spec, 0, torch.arange(n))
+    torch.cuda.synchronize()
+    _check_against_cpu(raw, spec, out)
+
+
+def test_streaming_decode_flags_corruption_at_the_payload_edges():
+    spec = CacheSpec(layers=1, kv_heads=8, head_dim=128, block_tokens=128, bits=4, group_size=32)
+    raw = _encoded(spec, 9, 7)
+    scales, codes = 128 * 8 * 4 * 2, 128 * 8 * 64       # bytes per section
+    end = HEADER.size + 2 * scales + 2 * codes            # header + payload
+    bad = raw.clone()
+    bad[0, HEADER.size] ^= 0x01             # first payload byte
+    bad[1, end - 1] ^= 0x80                 # last payload byte
+    bad[2, end] ^= 0xFF                     # padding after the payload: outside the CRC
+    bad[3, HEADER.size + 2 * scales] ^= 0x10  # first byte of the K codes
+    bad[4, 0] = ord("Y")                    # magic: not copied, valid 0
+    bad[5, 48] ^= 0x01                      # the stored CRC itself
+    bad[6, 16] ^= 0x01                      # block id
+    out = [t.cpu() for t in ops.decode_records(bad.to(DEV), spec, 0, torch.arange(9))]
+    status = out[5].tolist()
+    crc, hdr, bid = ops.RECORD_BAD_CRC, ops.RECORD_BAD_HEADER, ops.RECORD_BAD_ID
+    assert status[:4] == [crc, crc, 0, crc]
+    assert status[4] & hdr and int(out[4][4]) == 0
+    assert status[5:] == [crc, bid, 0, 0]
+    for i in (0, 1, 2, 3, 5, 6, 7, 8):  # copied whatever the CRC says
+        blk = decode_record(bad[i].clone(), spec, verify_crc=False)
+        assert torch.equal(out[0][i], blk.key.packed) and torch.equal(out[1][i], blk.value.packed)
+        assert torch.equal(out[2][i].view(torch.int16), blk.key.scales.view(torch.int16))
+        assert torch.equal(out[3][i].view(torch.int16), blk.value.scales.view(torch.int16))
+        assert int(out[4][i]) == blk.valid_tokens
+
+
+def test_unaligned_records_take_the_per_record_kernel_with_the_same_result():
+    spec = CacheSpec(layers=1, kv_heads=8, head_dim=128, block_tokens=128, bits=4, group_size=32)
+    raw = _encoded(spec, 5, 11)
+    aligned = ops.decode_records(raw.to(DEV), spec, 0)
+    flat = torch.zeros(raw.numel() + 4, dtype=torch.uint8, device=DEV)
+    flat[4:] = raw.reshape(-1).to(DEV)
+    shifted = ops.decode_records(flat[4:], spec, 0)    # 4-byte aligned, not 16
+    torch.cuda.synchronize()
+    for a, b in zip(aligned, shifted):
+        assert torch.equal(a, b)
+    _check_against_cpu(raw, spec, shifted)
