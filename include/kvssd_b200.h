@@ -88,10 +88,12 @@ KVSSD_B200_API int kvssd_b200_decode_workspace_size(int n_sel_blocks, int block_
  * valid_tokens entries are never dereferenced: they are skipped/clamped and recorded in the
  * workspace status word (see kvssd_b200_read_status). Outputs: out, lse as in the header.
  * The workspace (>= kvssd_b200_decode_workspace_size bytes, 16-byte aligned) starts with a
- * 2048-byte header holding that sticky status word and the counters of the fused combine
- * (the streaming kernel folds its split-KV parts itself; the counters return to zero at the
- * end of every call): zero the header once after allocating the workspace. Calls
- * sharing one workspace must be ordered on the GPU (same stream or explicit events). */
+ * 2048-byte header holding that sticky status word and the call epoch of the fused combine
+ * (the streaming kernel folds its split-KV parts itself: every part value is written with the
+ * call's epoch beside it and the folding CTAs poll the values), followed by the parts: zero
+ * the WHOLE workspace once after allocating it, so that no leftover word carries a future
+ * epoch. Calls sharing one workspace must be ordered on the GPU (same stream or explicit
+ * events). */
 KVSSD_B200_API int kvssd_b200_decode(const void* query, int query_dtype, const uint8_t* packed_k,
                       const uint8_t* packed_v, const uint16_t* scales_k,
                       const uint16_t* scales_v, const int32_t* valid_tokens,
@@ -111,15 +113,14 @@ KVSSD_B200_API int kvssd_b200_decode(const void* query, int query_dtype, const u
  * without a device allocator of their own (a plain C, cgo or JNI host), and serving loops
  * that must not call cudaMalloc/cudaFree there, which synchronise the device.
  * Limits: a geometry whose plan needs more than KVSSD_B200_STATIC_SCRATCH_BYTES (2048 bytes of
- * header plus n_parts * query_heads * (head_dim + 2) * 4; the c2 shape needs 2.5 MB) is
+ * header plus n_parts * query_heads * (head_dim + 2) * 8; the c2 shape needs 4.9 MB) is
  * rejected with KVSSD_B200_ERR_WORKSPACE before anything is launched. The first call on each
- * device resolves the scratch address and zeroes its 2048-byte header (the only part
- * that must start at zero) on `stream`; make that first call before any stream capture.
- * The address is kept per device and driver context: after cudaDeviceReset the next call
- * (again before any capture) sets the new context's scratch up the same way. After a call
- * that flagged a wait that gave up (status bits 4, 8 or 32), call kvssd_b200_read_status on
- * the scratch with clear = 1: it re-zeroes the whole header, including the arrival counters
- * a late CTA may have left behind.
+ * device resolves the scratch address and zeroes the scratch on `stream`; make that first call
+ * before any stream capture. The address is kept per device and driver context: after
+ * cudaDeviceReset the next call (again before any capture) sets the new context's scratch up
+ * the same way. After a call that flagged a wait that gave up (status bits 4, 8 or 32), call
+ * kvssd_b200_read_status on the scratch with clear = 1: it zeroes the sticky word, and the
+ * next call is good again.
  * Every call on a device uses the same scratch, so calls on one device must not overlap in
  * time (one stream, or events between streams): overlapping calls race on the parts.
  * If `scratch` is not NULL it receives the scratch address, which kvssd_b200_read_status
@@ -223,8 +224,7 @@ KVSSD_B200_API int kvssd_b200_decode_batched_workspace_size(int n_problems, int 
  * descriptor contents). The grid gets floor(SMs / n_problems) CTAs per problem (at least 1);
  * each problem's split-KV parts are folded by its own CTAs in the grid's tail. Needs the
  * streaming kernel's shapes (INT4, head_dim 128, group 32 or 64, 16-byte aligned operands)
- * and n_problems <= the SM count; workspace as kvssd_b200_decode (zero its 2048-byte header
- * once). Amortises the per-decode tail and launch over a multi-layer step or a batch of
+ * and n_problems <= the SM count; workspace as kvssd_b200_decode (zero it once). Amortises the per-decode tail and launch over a multi-layer step or a batch of
  * sequences (the reference decodes one layer per call, src/kvssd/pipeline.py:167-187). No
  * reference counterpart. */
 KVSSD_B200_API int kvssd_b200_decode_batched(const kvssd_b200_problem* problems, int n_problems,
@@ -285,9 +285,9 @@ KVSSD_B200_API int kvssd_b200_decode_exchange(const void* query, int query_dtype
  * for another rank, 16 = a batched problem descriptor was refused, 32 = a TMA-fed kernel gave
  * up waiting for its copies). After bits 4, 8 or 32 the kernels write NaN into out and lse of
  * that call and of every later call on the workspace until the word is cleared, so a failure
- * is never returned as a plausible number. clear = 1 with a nonzero word re-zeroes the
- * workspace's whole 2048-byte header (status word and arrival counters), which makes the
- * workspace usable again. Returns KVSSD_B200_ERR_DEVICE_STATUS when the word is nonzero. No
+ * is never returned as a plausible number. clear = 1 with a nonzero word zeroes the word
+ * (and the fused combine's test hook), which makes the workspace usable again; the epoch is
+ * kept, since the parts of earlier calls carry older ones. Returns KVSSD_B200_ERR_DEVICE_STATUS when the word is nonzero. No
  * reference counterpart (the reference raises through TORCH_CHECK,
  * csrc/fused_decode.cu:141). */
 KVSSD_B200_API int kvssd_b200_read_status(void* workspace, int clear, unsigned* device_status,

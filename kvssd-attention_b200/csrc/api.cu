@@ -58,12 +58,14 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(KVSSD_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-// Workspace header, zeroed once by the caller and zero again after every call: the device
-// status word (byte 0), the fused combine's arrival and combiner counters (byte 128) and the
-// batched decode's pair per problem (byte 256, up to 148 problems).
+// Workspace: a 2048-byte header, then the split-KV parts. The caller zeroes the whole
+// workspace once after allocating it. Header: the device status word (byte 0) and the fused
+// combine's words (byte 128): the epoch of the last call, the test hook (zero in use) and the
+// batched combiners' counter (zero between calls). With the fused combine every part value is
+// a tagged 64-bit word {f32 value, epoch tag} (combine.cuh), so the parts take 8 bytes a value;
+// the separate combine launch reads the same region as plain f32.
 constexpr size_t kHeaderBytes = 2048;
 constexpr size_t kTicketOffset = 128;
-constexpr size_t kProblemTicketOffset = 256;
 constexpr int kMaxParts = 8192;       // bound on split-KV parts
 
 struct DeviceInfo {
@@ -228,8 +230,8 @@ int make_plan(const Geometry& g, bool aligned, bool allow_stream, Plan& p,
   splits = std::min<long long>(splits, kMaxParts / parts_per_split);
   p.n_splits = static_cast<int>(splits);
   p.n_parts = p.n_splits * parts_per_split;
-  const size_t part_floats = static_cast<size_t>(p.n_parts) * g.qh * (g.d + 2);
-  p.ws_bytes = kHeaderBytes + part_floats * sizeof(float);
+  const size_t part_values = static_cast<size_t>(p.n_parts) * g.qh * (g.d + 2);
+  p.ws_bytes = kHeaderBytes + part_values * sizeof(unsigned long long);
   return KVSSD_B200_OK;
 }
 
@@ -383,7 +385,7 @@ int prepare_decode(const void* query, int query_dtype, const uint8_t* packed_k,
   a.score_scale = sm_scale * 1.4426950408889634f;  // log2(e): scores kept in log2 units
   char* ws = static_cast<char*>(workspace);
   a.status = reinterpret_cast<unsigned*>(ws);
-  a.tickets = reinterpret_cast<unsigned*>(ws + kTicketOffset);
+  a.part_epoch = reinterpret_cast<unsigned*>(ws + kTicketOffset);
   a.fuse_combine = 0;
   a.out = nullptr;
   a.lse = nullptr;
@@ -392,6 +394,8 @@ int prepare_decode(const void* query, int query_dtype, const uint8_t* packed_k,
   for (int r = 0; r < kMaxExchangeRanks; ++r) a.xpeers[r] = nullptr;
   a.part_ml = reinterpret_cast<float*>(ws + kHeaderBytes);
   a.part_acc = a.part_ml + static_cast<size_t>(p.n_parts) * query_heads * 2;
+  a.tpart_acc = reinterpret_cast<unsigned long long*>(ws + kHeaderBytes) +
+                static_cast<size_t>(p.n_parts) * query_heads * 2;
   return KVSSD_B200_OK;
 }
 
@@ -545,7 +549,7 @@ unsigned long long current_context_id() {
 }
 
 // Address of the current device's scratch. The first call per device and context resolves
-// the symbol (with the device current) and zeroes the status header on `s`; a later context
+// the symbol (with the device current) and zeroes the scratch on `s`; a later context
 // on the same device (after cudaDeviceReset) is a fresh module instance and is set up again.
 int static_scratch(cudaStream_t s, void** ptr) {
   int dev = 0;
@@ -562,8 +566,8 @@ int static_scratch(cudaStream_t s, void** ptr) {
     e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "static scratch address");
     if (slot.ptr == nullptr || slot.context != ctx || p != slot.ptr) {
-      e = cudaMemsetAsync(p, 0, kHeaderBytes, s);
-      if (e != cudaSuccess) return cuda_fail(e, "static scratch status clear");
+      e = cudaMemsetAsync(p, 0, KVSSD_B200_STATIC_SCRATCH_BYTES, s);  // header and part tags
+      if (e != cudaSuccess) return cuda_fail(e, "static scratch clear");
     }
     slot.ptr = p;
     slot.context = ctx;
@@ -855,10 +859,8 @@ int plan_batched(int n_problems, int block_tokens, int query_heads, int kv_heads
   bp.ctas = std::max(1, info.sms / n_problems);
   p.n_splits = bp.ctas;
   p.n_parts = bp.ctas * n_problems;
-  if (kProblemTicketOffset + static_cast<size_t>(2) * n_problems * sizeof(unsigned) > kHeaderBytes)
-    return fail(KVSSD_B200_ERR_UNSUPPORTED, "too many problems for the workspace header");
-  bp.ws_bytes = kHeaderBytes +
-                static_cast<size_t>(p.n_parts) * query_heads * (head_dim + 2) * sizeof(float);
+  bp.ws_bytes = kHeaderBytes + static_cast<size_t>(p.n_parts) * query_heads * (head_dim + 2) *
+                                  sizeof(unsigned long long);
   return KVSSD_B200_OK;
 }
 
@@ -915,9 +917,11 @@ int kvssd_b200_decode_batched(const kvssd_b200_problem* problems, int n_problems
   a.score_scale = sm_scale * 1.4426950408889634f;
   char* ws = static_cast<char*>(workspace);
   a.status = reinterpret_cast<unsigned*>(ws);
-  a.problem_tickets = reinterpret_cast<unsigned*>(ws + kProblemTicketOffset);
+  a.part_epoch = reinterpret_cast<unsigned*>(ws + kTicketOffset);
   a.part_ml = reinterpret_cast<float*>(ws + kHeaderBytes);
   a.part_acc = a.part_ml + static_cast<size_t>(p.n_parts) * query_heads * 2;
+  a.tpart_acc = reinterpret_cast<unsigned long long*>(ws + kHeaderBytes) +
+                static_cast<size_t>(p.n_parts) * query_heads * 2;
   a.problems = problems;
   a.fuse_combine = 1;
   {
@@ -953,10 +957,11 @@ int kvssd_b200_read_status(void* workspace, int clear, unsigned* device_status,
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return cuda_fail(e, "status read");
   if (clear && host) {
-    // The whole header: after a timed-out wait, a CTA that arrived late may have left an
-    // arrival counter off zero, which would make the next call's combine start early. The
-    // stream has drained above, so no kernel of this workspace is running.
-    e = cudaMemsetAsync(workspace, 0, kHeaderBytes, s);
+    // The status word and the combine's test hook (the stream has drained above, so no kernel
+    // of this workspace is running). The epoch stays: parts of earlier calls carry older tags.
+    e = cudaMemsetAsync(workspace, 0, sizeof(unsigned), s);
+    if (e == cudaSuccess)
+      e = cudaMemsetAsync(static_cast<char*>(workspace) + kTicketOffset + 4, 0, 8, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(e, "status clear");
   }

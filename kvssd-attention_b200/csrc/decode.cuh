@@ -40,12 +40,19 @@ struct DecodeArgs {
   long long total_tiles;
   int n_splits;
   float score_scale;  // sm_scale * log2(e): scores are kept in the log2 domain
-  float* part_acc;    // [n_parts, qh, d] unnormalised sum p*v
-  float* part_ml;     // [n_parts, qh, 2]  (running max in log2 domain, sum of p)
+  // Parts: plain f32 [n_parts, qh, 2] (running max in log2 domain, sum of p) at part_ml and
+  // [n_parts, qh, d] (unnormalised sum p*v) at part_acc when the combine is a separate launch;
+  // with the fused combine the same arrays as tagged 64-bit words (combine.cuh), the (m, l)
+  // words at part_ml and the sums at tpart_acc.
+  float* part_acc;
+  float* part_ml;
+  unsigned long long* tpart_acc;
   unsigned* status;   // device status word (DeviceStatusBits)
   // Fused combine (streaming kernel): the last CTAs to finish fold all parts into out/lse.
   int fuse_combine;
-  unsigned* tickets;  // [0] CTAs that wrote their part, [1] combiners done; zero between calls
+  // Header words of the fused combine: [0] epoch of the last call, [1] test hook (0 in use),
+  // [2] combiners done (batched calls; 0 between calls). See fused_tail.cuh.
+  unsigned* part_epoch;
   float* out;         // [qh, d] normalised output
   float* lse;         // [qh] natural-log LSE
   // Cross-GPU exchange (token-range shards, fused combine only): every combiner pushes its
@@ -54,9 +61,8 @@ struct DecodeArgs {
   int xrank;
   uint8_t* xpeers[kMaxExchangeRanks];  // every rank's exchange buffer ([xrank] is local)
   // Batched decode: problem blockIdx.y of this device array (nullptr: one problem, the
-  // fields above); each problem's tickets are 2 words at problem_tickets + 2 * problem.
+  // fields above).
   const kvssd_b200_problem* problems;
-  unsigned* problem_tickets;
 };
 
 // Exchange buffer layout for `world` ranks and n_slices = qh * ceil(d / 32) slices:

@@ -115,6 +115,8 @@ __device__ __forceinline__ void async_decode_body(const DecodeArgs& a) {
   // Exchange epoch of this call (completed calls + 1), read before this CTA's arrival.
   const unsigned epoch =
       a.xworld ? *reinterpret_cast<const volatile unsigned*>(a.xpeers[a.xrank]) + 1u : 0u;
+  // The call's part tags (fused combine), read before this CTA's part is written.
+  const PartEpoch pe = a.fuse_combine ? read_part_epoch(a) : PartEpoch{0u, 0u, false};
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, c = lane & 3;
   const int h = warp % KVH, sub = warp / KVH;
@@ -219,8 +221,9 @@ __device__ __forceinline__ void async_decode_body(const DecodeArgs& a) {
   finish_stream<GROUP, false>(state, c);
   cp_async_wait<0>();
   __syncthreads();
-  merge_warps_write_part<KVH>(a, reinterpret_cast<float*>(smem), warp, lane, q0, nq, state);
-  if (a.fuse_combine) fused_combine_tail<D>(a, epoch, a.n_splits);
+  merge_warps_write_part<KVH>(a, reinterpret_cast<float*>(smem), warp, lane, q0, nq, state,
+                              pe.epoch | (pe.poison ? kTagPoison : 0u));
+  if (a.fuse_combine) fused_combine_tail<D>(a, epoch, pe, a.n_splits);
 }
 
 template <int KVH, int GROUP>
@@ -247,6 +250,10 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_batched_kernel(
       (reinterpret_cast<uintptr_t>(pd.query) % qsize) || pd.n_pool_blocks < 1 ||
       pd.n_sel_blocks < 0) {
     if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.status, kDevBadProblem);
+    // A combining CTA of the refused problem still counts itself for the epoch store.
+    const int n_comb = min(a.n_splits, a.qh * ((a.d + 31) / 32));
+    if (threadIdx.x == 0 && static_cast<int>(blockIdx.x) >= a.n_splits - n_comb)
+      publish_part_epoch(a, 0u, n_comb);
     return;
   }
   DecodeArgs b = a;
@@ -262,10 +269,10 @@ __global__ void __launch_bounds__(kAsyncThreads, 1) async_decode_batched_kernel(
   b.total_tiles = static_cast<long long>(pd.n_sel_blocks) * a.tiles_per_block;
   b.out = pd.out;
   b.lse = pd.lse;
+  // This problem's slice of the (tagged, 64-bit) part arrays; the epoch is the grid's.
   const size_t parts = static_cast<size_t>(blockIdx.y) * a.n_splits * a.qh;
-  b.part_ml = a.part_ml + parts * 2;
-  b.part_acc = a.part_acc + parts * a.d;
-  b.tickets = a.problem_tickets + 2 * blockIdx.y;
+  b.part_ml = a.part_ml + parts * 4;
+  b.tpart_acc = a.tpart_acc + parts * a.d;
   async_decode_body<KVH, GROUP>(b);
 }
 

@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP, BITS>::THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[L::NS], empty[L::NS];
   __shared__ int stage_rows[L::NS];
+  __shared__ int cta_fault;  // a wait of this CTA gave up: its part is poisoned
   __shared__ __align__(8) uint64_t q_bar;  // the staged query copy has landed
   const uint32_t raw_s = smem_addr(smem_raw);
   const uint32_t ring_s = (raw_s + 1023u) & ~1023u;
@@ -87,6 +88,7 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP, BITS>::THREADS, 1)
   const int h = warp % KVH, grp = warp / KVH;
   // Shared-memory and parameter-space setup may overlap the preceding grid's tail.
   if (threadIdx.x == 0) {
+    cta_fault = 0;
     for (int s = 0; s < L::NS; ++s) {
       mbar_init(smem_addr(&full[s]), 1);
       mbar_init(smem_addr(&empty[s]), KVH);
@@ -113,6 +115,14 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP, BITS>::THREADS, 1)
   // Exchange epoch of this call (completed calls + 1), read before this CTA's arrival.
   const unsigned epoch =
       a.xworld ? *reinterpret_cast<const volatile unsigned*>(a.xpeers[a.xrank]) + 1u : 0u;
+  // The call's part tags (fused combine): read by producer 0 once it has issued its stages
+  // (before this CTA's part is written) into shared memory, out of the streaming loop's
+  // registers and off the start-up path.
+  __shared__ PartEpoch s_pe;
+  auto flag_timeout = [&]() {
+    atomicOr(a.status, kDevStreamTimeout);
+    cta_fault = 1;
+  };
   const unsigned long long deadline = global_ns() + kCombineWaitNs;
   __syncthreads();
   if (q_staged && warp == kStreamWarps && lane == 0) {
@@ -141,7 +151,7 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP, BITS>::THREADS, 1)
                                              ((i / kTmaSlots) & 1) ^ 1, deadline,
                                              kTmaMaxPolls);
       if (!__all_sync(0xffffffffu, free_slot)) {  // the warp leaves together
-        if (lane == 0) atomicOr(a.status, kDevStreamTimeout);
+        if (lane == 0) flag_timeout();
         break;
       }
       issued = i + 1;
@@ -173,13 +183,15 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP, BITS>::THREADS, 1)
       }
       __syncwarp();
     }
+    if (pi == 0 && lane == 0)
+      s_pe = a.fuse_combine ? read_part_epoch(a) : PartEpoch{0u, 0u, false};
   } else {
     // ---------------- consumers
     bool q_ready = true;
     if (q_staged)
       q_ready = __all_sync(0xffffffffu,
                            mbar_wait_until(smem_addr(&q_bar), 0, deadline, kTmaMaxPolls));
-    if (!q_ready && lane == 0) atomicOr(a.status, kDevStreamTimeout);
+    if (!q_ready && lane == 0) flag_timeout();
     const void* qsrc = q_staged && q_ready ? static_cast<const void*>(q_smem) : a.q;
     const uint32_t hs = static_cast<uint32_t>(h * 2 * G);  // head's byte offset in a scale row
     const uint32_t sk_off = L::swizzled(g * L::SRB + hs);
@@ -192,7 +204,7 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP, BITS>::THREADS, 1)
       const bool landed =
           mbar_wait_until(smem_addr(&full[sl]), (i / kTmaSlots) & 1, deadline, kTmaMaxPolls);
       if (__all_sync(0xffffffffu, landed)) return true;
-      if (lane == 0) atomicOr(a.status, kDevStreamTimeout);
+      if (lane == 0) flag_timeout();
       return false;
     };
     if constexpr (BITS == 4) {
@@ -261,16 +273,19 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP, BITS>::THREADS, 1)
     // is reused and the CTA exits.
     const unsigned long long drain_deadline = global_ns() + kCombineWaitNs;
     if (pi == 0 && q_staged && !mbar_wait_until(smem_addr(&q_bar), 0, drain_deadline, kTmaMaxPolls))
-      atomicOr(a.status, kDevStreamTimeout);
+      flag_timeout();
     for (int idx = max(0, issued - kTmaSlots); idx < issued; ++idx)
       if (idx % L::PPG == pp &&
           !mbar_wait_until(smem_addr(&full[gp * kTmaSlots + idx % kTmaSlots]),
                            (idx / kTmaSlots) & 1, drain_deadline, kTmaMaxPolls))
-        atomicOr(a.status, kDevStreamTimeout);
+        flag_timeout();
   }
   __syncthreads();
-  merge_warps_write_part<KVH, BITS>(a, reinterpret_cast<float*>(ring), warp, lane, q0, nq, state);
-  if (a.fuse_combine) fused_combine_tail<D>(a, epoch, a.n_splits);
+  const PartEpoch pe = s_pe;
+  const unsigned tag = pe.epoch | (pe.poison || cta_fault ? kTagPoison : 0u);
+  merge_warps_write_part<KVH, BITS>(a, reinterpret_cast<float*>(ring), warp, lane, q0, nq, state,
+                                    tag);
+  if (a.fuse_combine) fused_combine_tail<D>(a, epoch, pe, a.n_splits);
 }
 
 using TmaKernel = void (*)(const DecodeArgs, const TmaMaps);

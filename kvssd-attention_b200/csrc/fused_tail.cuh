@@ -9,10 +9,6 @@
 
 namespace kvb {
 
-// Bounds of a fused-combine wait: one second of GPU time, and a poll count as a second guard.
-constexpr unsigned long long kCombineWaitNs = 1000000000ull;
-constexpr unsigned kCombineMaxPolls = 1u << 26;
-
 // Cross-GPU exchange of one combined slice, run by warp 0 of the CTA that combined it (token-
 // range shards of one context, one rank per GPU). Every value travels as one 64-bit word
 // {value, epoch} written with a single store into buffer half (epoch & 1) of every rank's
@@ -90,82 +86,110 @@ __device__ __forceinline__ void exchange_slice(const DecodeArgs& a, unsigned epo
     a.lse[h] = bad ? nan_f32() : empty ? -INFINITY : (M + log2f(den)) * kLn2;
 }
 
+// The call's part tags, read by every CTA at its start (after the preceding grid): epoch =
+// the header's previous epoch + 1; expect0 = the tag the combiners expect of part 0 (the
+// epoch, unless the header's test hook word is nonzero: then epoch + hook, which no CTA
+// writes, so the combine waits out its bound); poison: the status word already holds a fatal
+// bit (an earlier call on this workspace failed and nobody has cleared it).
+struct PartEpoch {
+  unsigned epoch;
+  unsigned expect0;
+  bool poison;
+};
+
+__device__ __forceinline__ PartEpoch read_part_epoch(const DecodeArgs& a) {
+  PartEpoch pe;
+  const unsigned prev = *reinterpret_cast<const volatile unsigned*>(a.part_epoch);
+  const unsigned hook = *reinterpret_cast<const volatile unsigned*>(a.part_epoch + 1);
+  pe.epoch = next_epoch(prev);
+  pe.expect0 = hook ? next_epoch(prev + hook) : pe.epoch;
+  pe.poison = (*reinterpret_cast<const volatile unsigned*>(a.status) & kDevFatalBits) != 0u;
+  return pe;
+}
+
+// Stores the call's epoch in the header (and clears the test hook), by thread 0 of a
+// combining CTA after its fold. One problem: every combiner stores it (all CTAs of the call
+// read the header before writing the parts the combiner waited for). Batched: the problems'
+// CTAs share the epoch, and a problem's combiners only wait for their own problem's parts, so
+// the last combiner of the whole grid (counted in header word 2, re-armed by that combiner)
+// stores it. epoch 0: a CTA of a refused problem that read nothing (the header still holds
+// the previous call's epoch when it is the last).
+__device__ __forceinline__ void publish_part_epoch(const DecodeArgs& a, unsigned epoch,
+                                                   int n_comb) {
+  if (a.problems != nullptr) {
+    const unsigned total = gridDim.y * static_cast<unsigned>(n_comb);
+    if (atomicAdd(a.part_epoch + 2, 1u) != total - 1u) return;
+    a.part_epoch[2] = 0u;
+    if (epoch == 0u) epoch = next_epoch(*reinterpret_cast<const volatile unsigned*>(a.part_epoch));
+  }
+  a.part_epoch[0] = epoch;
+  a.part_epoch[1] = 0u;
+}
+
 // Fused split-KV combine at the end of the decode grid (launched cooperatively, so all CTAs
-// are co-resident). Every CTA publishes its part and signals its arrival with one release add
-// on tickets[0]; the n_comb highest-numbered CTAs (one per (query head, 32-dim) slice, or
-// fewer when the grid is smaller) wait until all n_splits parts have arrived and fold one or
-// more slices each. Each combiner counts itself on tickets[1] as soon as it has seen every
-// arrival -- the atomic's round trip overlaps its fold -- and the last one re-arms both
-// counters (zero again for the next call) and publishes the exchange epoch after its fold.
-// The wait is bounded: on timeout the CTA flags kDevCombineTimeout and carries on. A combiner
-// that timed out, or that finds a fatal bit in the status word once every part has arrived
-// (another CTA gave up on its copies, or an earlier call on this workspace failed and nobody
-// has cleared the word), writes NaN into its slices of out and lse.
+// are co-resident). Every CTA has written its part as tagged words (merge_warps_write_part);
+// the n_comb highest-numbered CTAs (one per (query head, 32-dim) slice, or fewer when the grid
+// is smaller) poll the parts of their slices until every word carries this call's epoch and
+// fold them (combine_slice_tagged). A combiner that timed out or met a poisoned part writes
+// NaN into its slices of out and lse (and flags kDevCombineTimeout on timeout). Each combiner
+// then stores the call's epoch in the header and clears the test hook: every CTA of the call
+// read them at its start, before writing the part this combiner waited for.
 template <int D>
-__device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned epoch,
-                                                   int n_parts) {
-  __shared__ int poison_flag;
-  __syncthreads();  // every warp's part stores precede the CTA's release below
+__device__ __forceinline__ void fused_combine_tail(const DecodeArgs& a, unsigned xepoch,
+                                                   const PartEpoch& pe, int n_parts) {
   constexpr int kChunks = (D + 31) / 32;
   const int n_slices = a.qh * kChunks;
   const int n_comb = min(a.n_splits, n_slices);
   const int k = static_cast<int>(blockIdx.x) - (a.n_splits - n_comb);
-  if (threadIdx.x == 0) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.tickets) : "memory");
-    if (k >= 0) {
-      const unsigned long long t0 = global_ns();
-      unsigned polls = 0;
-      bool timed_out = false;
-      // Signed: a counter left below zero (a corrupted workspace header) reads as "parts
-      // missing" to every combiner, so all of them wait out the bound and fail closed together
-      // instead of some folding early.
-      while (static_cast<int>(ld_acquire_gpu(a.tickets)) < a.n_splits) {
-        if (++polls > kCombineMaxPolls || global_ns() - t0 > kCombineWaitNs) {
-          atomicOr(a.status, kDevCombineTimeout);
-          timed_out = true;
-          break;
-        }
-        __nanosleep(32);
-      }
-      poison_flag = timed_out || (ld_acquire_gpu(a.status) & kDevFatalBits) != 0u;
-    }
-  }
   if (k < 0) return;
-  __syncthreads();
-  const bool poison = poison_flag != 0;
-  // Every combiner has passed its wait when tickets[1] reaches n_comb; the returned count is
-  // only needed after the fold.
-  unsigned combined_before = 0u;
-  if (threadIdx.x == 0) combined_before = atomicAdd(a.tickets + 1, 1u);
+  const unsigned long long* tml = reinterpret_cast<const unsigned long long*>(a.part_ml);
+  const unsigned long long* tacc = a.tpart_acc;
+  TagWait w{global_ns() + kCombineWaitNs, false, false};
   if (a.xworld == 0 && n_parts <= 32) {
     // Few parts (a batched problem's handful of CTAs): one warp folds a whole slice, so the
     // CTA's 16 warps work on 16 of its slices at once.
-    const int warp = threadIdx.x >> 5, n_warps = blockDim.x >> 5;
+    const int warp = threadIdx.x >> 5, n_warps = blockDim.x >> 5, lane = threadIdx.x & 31;
     const int mine = (n_slices - k + n_comb - 1) / n_comb;  // slices k, k + n_comb, ...
+    bool gave_up = false;
     for (int j = warp; j < mine; j += n_warps) {
-      const int sl = k + j * n_comb;
-      combine_slice_warp(a.part_acc, a.part_ml, n_parts, a.qh, D, sl / kChunks, sl % kChunks,
-                         a.out, a.lse, poison);
+      const int sl = k + j * n_comb, h = sl / kChunks, chunk = sl % kChunks;
+      const int dd = chunk * 32 + lane;
+      TagWait ww{w.deadline, false, false};
+      float M = -INFINITY, L = 0.f, A = 0.f;
+      fold_tagged_warp(tml, tacc, 0, n_parts, a.qh, D, h, dd, pe.epoch, pe.expect0, ww, M, L,
+                       A);
+      gave_up |= ww.timed_out;
+      const bool bad = ww.timed_out || ww.poison || pe.poison;
+      const bool empty = M == -INFINITY || !(L > 0.f);
+      if (dd < D) a.out[static_cast<size_t>(h) * D + dd] = bad ? nan_f32() : empty ? 0.f : A / L;
+      if (chunk == 0 && lane == 0)
+        a.lse[h] = bad ? nan_f32() : empty ? -INFINITY : (M + log2f(L)) * kLn2;
     }
-    __syncthreads();
+    if (__syncthreads_or(gave_up) && threadIdx.x == 0) atomicOr(a.status, kDevCombineTimeout);
   } else {
-  for (int sl = k; sl < n_slices; sl += n_comb) {
-    if (a.xworld == 0) {
-      combine_slice(a.part_acc, a.part_ml, n_parts, a.qh, D, sl / kChunks, sl % kChunks,
-                    a.out, a.lse, poison);
-    } else {
+    for (int sl = k; sl < n_slices; sl += n_comb) {
       float o = 0.f, l2 = -INFINITY;
-      combine_slice_result(a.part_acc, a.part_ml, n_parts, a.qh, D, sl / kChunks,
-                           sl % kChunks, &o, &l2);
-      if (threadIdx.x < 32) exchange_slice<D>(a, epoch, sl, n_slices, o, l2, poison);
+      combine_slice_tagged(tml, tacc, n_parts, a.qh, D, sl / kChunks, sl % kChunks, pe.epoch,
+                           pe.expect0, w, &o, &l2);
+      const bool poison = w.timed_out || w.poison || pe.poison;
+      if (threadIdx.x < 32) {
+        const int lane = threadIdx.x, chunk = sl % kChunks, h = sl / kChunks;
+        if (a.xworld == 0) {
+          const int dd = chunk * 32 + lane;
+          if (dd < D) a.out[static_cast<size_t>(h) * D + dd] = poison ? nan_f32() : o;
+          if (chunk == 0 && lane == 0) a.lse[h] = poison ? nan_f32() : l2 * kLn2;
+        } else {
+          exchange_slice<D>(a, xepoch, sl, n_slices, o, l2, poison);
+        }
+      }
+      // after a timeout the later slices stop at their first poll (the deadline has passed)
     }
+    if (w.timed_out && threadIdx.x == 0) atomicOr(a.status, kDevCombineTimeout);
   }
-  }
-  if (threadIdx.x == 0 && combined_before == static_cast<unsigned>(n_comb) - 1) {
-    atomicExch(a.tickets, 0u);
-    atomicExch(a.tickets + 1, 0u);
-    // every CTA read the epoch at its start, before its arrival: publish the completed call
-    if (a.xworld) *reinterpret_cast<volatile unsigned*>(a.xpeers[a.xrank]) = epoch;
+  if (threadIdx.x == 0) {
+    publish_part_epoch(a, pe.epoch, n_comb);
+    // every CTA read the exchange epoch at its start, before its part: publish the call
+    if (a.xworld) *reinterpret_cast<volatile unsigned*>(a.xpeers[a.xrank]) = xepoch;
   }
 }
 

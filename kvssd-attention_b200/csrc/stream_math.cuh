@@ -29,6 +29,7 @@
 //   running max by 2^8, detected with one warp vote per tile.
 #pragma once
 
+#include "combine.cuh"
 #include "decode_tc.cuh"
 
 namespace kvb {
@@ -467,7 +468,7 @@ __host__ __device__ constexpr size_t stream_merge_bytes(int kvh) {
 template <int KVH, int BITS = 4>
 __device__ __forceinline__ void merge_warps_write_part(const DecodeArgs& a, float* buf, int warp,
                                                        int lane, int q0, int nq,
-                                                       StreamState& s) {
+                                                       StreamState& s, unsigned tag) {
   constexpr int kFields = 4 + 4 * 8, WPH = kStreamWarps / KVH, D = 128;
   const int g = lane >> 2, c = lane & 3;
   const bool consumer = warp < kStreamWarps;
@@ -514,11 +515,23 @@ __device__ __forceinline__ void merge_warps_write_part(const DecodeArgs& a, floa
     const int n = 2 * c + hh;
     if (n >= nq) continue;
     const size_t row = static_cast<size_t>(blockIdx.x) * a.qh + (q0 + n);
+    const size_t col = (BITS == 4 ? 4 : 8) * g;
+    if (a.fuse_combine) {  // tagged words, polled by the fused combine
+      unsigned long long* tml = reinterpret_cast<unsigned long long*>(a.part_ml);
+      if (g == 0) st_tagged2(tml + row * 2, tag_word(s.m_run[hh], tag), tag_word(s.l_run[hh], tag));
+      unsigned long long* dst = a.tpart_acc + row * D + col;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int off = BITS == 4 ? 32 * (k >> 1) + 2 * (k & 1) : 64 * (k >> 2) + 2 * (k & 3);
+        st_tagged2(dst + off, tag_word(s.acc[k][hh], tag), tag_word(s.acc[k][2 + hh], tag));
+      }
+      continue;
+    }
     if (g == 0) {
       a.part_ml[row * 2 + 0] = s.m_run[hh];
       a.part_ml[row * 2 + 1] = s.l_run[hh];
     }
-    float* dst = a.part_acc + row * D + (BITS == 4 ? 4 : 8) * g;
+    float* dst = a.part_acc + row * D + col;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int off = BITS == 4 ? 32 * (k >> 1) + 2 * (k & 1) : 64 * (k >> 2) + 2 * (k & 3);

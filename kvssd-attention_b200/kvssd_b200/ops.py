@@ -28,8 +28,9 @@ _WORKSPACE_HEADER = 2048
 class _Workspaces:
     """Per-(device, stream) decode workspaces, grown on demand and reused across calls.
 
-    Reuse is safe because calls that share a workspace are ordered on one stream; the
-    header's device status word is zeroed once at allocation (it accumulates until read).
+    Reuse is safe because calls that share a workspace are ordered on one stream. A workspace
+    is zeroed once at allocation: the header's device status word (it accumulates until read),
+    the fused combine's epoch and the part words, whose epoch tags must not match a future call.
     """
 
     def __init__(self) -> None:
@@ -378,7 +379,7 @@ def decode_combine(workspace: torch.Tensor, n_parts: int, query_heads: int, head
 def read_device_status(device: torch.device | str | None = None, clear: bool = True,
                        stream: torch.cuda.Stream | None = None) -> int:
     """Synchronously reads the sticky device status word of the current (or given) stream's
-    workspace; ``clear`` re-zeroes the workspace header when the word is nonzero.
+    workspace; ``clear`` zeroes the word (and the fused combine's test hook) when it is nonzero.
 
     Bit 1: a block-table entry was outside the pool; bit 2: a valid_tokens entry was outside
     [0, block_tokens] (such entries are skipped/clamped by the kernels, never dereferenced);
@@ -463,7 +464,7 @@ class _StatusWatch:
     pinned host memory and records an event; ``poll()`` looks at the slots whose event has
     completed (no synchronisation) and ``check()`` waits for all of them. A failure is raised
     once, as DeviceFailure, after the word has been read and cleared on the device (which
-    re-zeroes the workspace header and makes the workspace usable again).
+    makes the workspace usable again).
     """
 
     SLOTS = 4

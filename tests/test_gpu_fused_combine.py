@@ -1,7 +1,7 @@
 """The streaming kernel's fused split-KV combine: equality with the two-launch path, the
-arrival counters returning to zero, and the bounded wait (a planted counter value that can
-never be reached makes the combining CTAs give up after about a second and flag status bit 4;
-nothing faults or hangs). A call that gave up returns NaN, later calls on the workspace return
+epoch advancing by one per call, and the bounded wait (the header's test hook makes the
+combining CTAs expect a tag of part 0 that no CTA writes, so they give up after about a second
+and flag status bit 4; nothing faults or hangs). A call that gave up returns NaN, later calls on the workspace return
 NaN until the status word is cleared, and the public entry points (the ``cuda`` backend's run,
 DeviceBlockPool) raise ops.DeviceFailure on the next call instead of returning a number."""
 
@@ -18,7 +18,16 @@ from kvssd_b200.workloads import WORKLOADS, make_layer
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
-TICKETS = 128  # byte offset of the two combine counters in the workspace header
+EPOCH = 128  # byte offset of the fused combine's epoch in the workspace header
+HOOK = 132   # the test hook word after it (zero in normal use)
+
+
+def _word(ws, off) -> int:
+    return int(ws[off:off + 4].cpu().view(torch.int32)[0])
+
+
+def _plant_hook(ws) -> None:
+    ws[HOOK:HOOK + 4] = torch.tensor([1, 0, 0, 0], dtype=torch.uint8, device=ws.device)
 
 
 @pytest.fixture(scope="module")
@@ -68,12 +77,12 @@ def test_streaming_plan_fuses_the_combine(layer):
     assert plan["kernel"] in ops.STREAMING_KERNELS
 
 
-def test_fused_combine_equals_two_launch_combine_and_resets_counters(layer):
+def test_fused_combine_equals_two_launch_combine_and_advances_the_epoch(layer):
     w, t = layer
     ws = _workspace(w, t)
     fused = _abi_decode(w, t, ws)
     torch.cuda.synchronize()
-    assert torch.count_nonzero(ws[TICKETS:TICKETS + 8]) == 0  # both counters re-armed
+    assert _word(ws, EPOCH) == 1 and _word(ws, HOOK) == 0  # a zeroed workspace starts at 1
     assert _status(ws) == 0
     args = (t[0], *t[1:], w.bits, w.group_size, 1.0 / math.sqrt(w.head_dim))
     n_parts, wsp = ops.decode_split(*args)
@@ -81,34 +90,32 @@ def test_fused_combine_equals_two_launch_combine_and_resets_counters(layer):
     torch.cuda.synchronize()
     torch.testing.assert_close(fused[0], two[0], atol=1e-6, rtol=1e-6)
     torch.testing.assert_close(fused[1], two[1], atol=1e-6, rtol=1e-6)
-    again = _abi_decode(w, t, ws)  # the counter was back at zero for the second call
-    torch.cuda.synchronize()
-    assert torch.equal(again[0], fused[0]) and torch.equal(again[1], fused[1])
+    for call in (2, 3):  # the parts of the previous call carry an older tag
+        again = _abi_decode(w, t, ws)
+        torch.cuda.synchronize()
+        assert _word(ws, EPOCH) == call
+        assert torch.equal(again[0], fused[0]) and torch.equal(again[1], fused[1])
 
 
 def test_fused_combine_wait_is_bounded_and_flagged(layer):
     w, t = layer
     ws = _workspace(w, t)
-    # Planted arrival count -100: after every CTA arrives the counter is still below the
-    # number of CTAs, so no combining CTA ever sees all parts.
-    ws[TICKETS:TICKETS + 4] = torch.tensor([0x9C, 0xFF, 0xFF, 0xFF], dtype=torch.uint8)
+    _abi_decode(w, t, ws)
+    _plant_hook(ws)  # part 0 is expected with a tag that no CTA writes
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     bad_out, bad_lse = _abi_decode(w, t, ws)
     torch.cuda.synchronize()
     elapsed = time.perf_counter() - t0
     assert torch.isnan(bad_out).all() and torch.isnan(bad_lse).all()
+    assert _word(ws, HOOK) == 0  # the combiners cleared the hook after giving up
     # the word is sticky: until it is cleared, every call on this workspace fails closed
     again_out, _ = _abi_decode(w, t, ws)
     torch.cuda.synchronize()
     assert torch.isnan(again_out).all()
     assert _status(ws) & 4
     assert elapsed < 30
-    # the last combiner re-armed both counters after the timeout: the next call on the same
-    # workspace is correct without the caller touching them
-    assert torch.count_nonzero(ws[TICKETS:TICKETS + 8]) == 0
-    ws[:4].zero_()  # the sticky status word is the caller's to clear
-    out, lse = _abi_decode(w, t, ws)
+    out, lse = _abi_decode(w, t, ws)  # _status cleared the word
     ref = ops.decode(*t, w.bits, w.group_size, 1.0 / math.sqrt(w.head_dim))
     torch.cuda.synchronize()
     assert _status(ws) == 0
@@ -116,10 +123,10 @@ def test_fused_combine_wait_is_bounded_and_flagged(layer):
 
 
 def _plant_unreachable_count(device=DEV):
-    """Plants the unreachable arrival count in the current stream's ops workspace."""
+    """Plants the test hook in the current stream's ops workspace: the next fused combine
+    waits for a part 0 tag that no CTA writes."""
     ws = ops._workspaces.get(device, torch.cuda.current_stream(device), 1 << 20)
-    ws[TICKETS:TICKETS + 4] = torch.tensor([0x9C, 0xFF, 0xFF, 0xFF], dtype=torch.uint8,
-                                           device=device)
+    _plant_hook(ws)
     torch.cuda.synchronize()
 
 

@@ -100,8 +100,8 @@ def test_static_scratch_recovers_after_a_wait_that_gave_up():
     _native.check(_static_decode(layer, w, out, lse, scratch), "kvssd_b200_decode_static")
     torch.cuda.synchronize()
     header = torch.as_tensor(_DeviceBytes(scratch.value, 2048), device="cuda")
-    # arrival count 2^32 - 100: the counter wraps below the CTA count, the combine gives up
-    header[128:132] = torch.tensor([0x9C, 0xFF, 0xFF, 0xFF], dtype=torch.uint8, device="cuda")
+    # the fused combine's test hook: part 0 is expected with a tag no CTA writes, it gives up
+    header[132:136] = torch.tensor([1, 0, 0, 0], dtype=torch.uint8, device="cuda")
     torch.cuda.synchronize()
     _native.check(_static_decode(layer, w, out, lse, scratch), "kvssd_b200_decode_static")
     torch.cuda.synchronize()
@@ -111,7 +111,8 @@ def test_static_scratch_recovers_after_a_wait_that_gave_up():
         scratch.value, 1, ctypes.byref(status), torch.cuda.current_stream().cuda_stream)
     assert rc == _native.ERR_DEVICE_STATUS and status.value & 4
     torch.cuda.synchronize()
-    assert torch.count_nonzero(header) == 0  # status word and counters re-zeroed
+    assert torch.count_nonzero(header[:4]) == 0  # status word cleared
+    assert torch.count_nonzero(header[132:140]) == 0  # hook and batched counter at zero
     for _ in range(2):
         _native.check(_static_decode(layer, w, out, lse, scratch), "kvssd_b200_decode_static")
         torch.cuda.synchronize()
