@@ -196,6 +196,26 @@ KVSSD_B200_API int kvssd_b200_read_records(const char* path, const long long* of
                                            int threads, int direct, int* used_direct);
 KVSSD_B200_API const char* kvssd_b200_io_last_error(void);
 
+/* GPUDirect Storage (cuFile) reads of whole records straight into device memory: kvssd's
+ * "gds" storage backend (src/kvssd/storage/gds.py:13-94 over csrc/gds_bindings.cpp:21-98,
+ * GDSFile: cuFileDriverOpen, O_DIRECT open, cuFileHandleRegister, cuFileRead). libcufile is
+ * loaded at run time; where it, its driver or an O_DIRECT descriptor is unavailable, open
+ * returns KVSSD_B200_ERR_UNSUPPORTED and kvssd_b200_gds_last_error gives the reason (the
+ * reference's probe() reports the same as unavailable). read_records reads n_records records
+ * of record_bytes (a multiple of 4096) at the 4096-aligned file offsets into
+ * device_destination + i * record_bytes (4096-byte aligned device memory), with up to
+ * `threads` reader threads; synchronous (the data is in device memory on return). Errors:
+ * KVSSD_B200_ERR_INVALID_ARGUMENT for misaligned requests, KVSSD_B200_ERR_CUDA for a failed or
+ * short cuFileRead (the reference raises OSError / EOFError). */
+typedef struct kvssd_b200_gds_file kvssd_b200_gds_file;
+KVSSD_B200_API int kvssd_b200_gds_open(const char* path, kvssd_b200_gds_file** file);
+KVSSD_B200_API int kvssd_b200_gds_read_records(kvssd_b200_gds_file* file,
+                                               const long long* offsets, int n_records,
+                                               size_t record_bytes, void* device_destination,
+                                               int threads);
+KVSSD_B200_API int kvssd_b200_gds_close(kvssd_b200_gds_file* file);
+KVSSD_B200_API const char* kvssd_b200_gds_last_error(void);
+
 /* One problem of a batched decode: its query [query_heads, head_dim], block pool
  * (PackedBatch layout), optional block table (NULL = all pool blocks in order) and outputs.
  * Problems of one batch share the geometry; their pools may be shared (a batch of sequences

@@ -26,6 +26,13 @@ from .pipeline import KVSSDPipeline
 from .pool import DeviceBlockPool
 from .quant import dequantize_tensor, quantize_tensor
 from .selectors import AllBlocks, RecentSinkBlocks
+from .storage import (
+    GDSStorageBackend,
+    StorageAvailability,
+    available_storage_backends,
+    register_storage_backend,
+    resolve_storage_backend,
+)
 from .store import KVCacheStore
 
 __all__ = [
@@ -33,10 +40,13 @@ __all__ = [
     "B200AttentionBackend",
     "CacheSpec",
     "DeviceBlockPool",
+    "GDSStorageBackend",
     "KVCacheStore",
     "KVSSDPipeline",
     "PackedBatch",
     "RecentSinkBlocks",
+    "StorageAvailability",
+    "available_storage_backends",
     "available_attention_backends",
     "dequantize_tensor",
     "fused_attention_tensors",
@@ -45,6 +55,8 @@ __all__ = [
     "packed_attention",
     "quantize_tensor",
     "register_attention_backend",
+    "register_storage_backend",
     "resolve_attention_backend",
+    "resolve_storage_backend",
     "stack_blocks",
 ]

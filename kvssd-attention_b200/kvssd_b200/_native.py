@@ -96,6 +96,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          ctypes.POINTER(_c_int)],
     ),
     "kvssd_b200_io_last_error": (ctypes.c_char_p, []),
+    "kvssd_b200_gds_open": (_c_int, [ctypes.c_char_p, ctypes.POINTER(_c_void)]),
+    "kvssd_b200_gds_read_records": (_c_int, [_c_void, _c_void, _c_int, _c_size, _c_void, _c_int]),
+    "kvssd_b200_gds_close": (_c_int, [_c_void]),
+    "kvssd_b200_gds_last_error": (ctypes.c_char_p, []),
     "kvssd_b200_exchange_bytes": (_c_int, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_size)]),
     "kvssd_b200_exchange_alloc": (_c_int, [_c_size, ctypes.POINTER(_c_void)]),
     "kvssd_b200_exchange_clear": (_c_int, [_c_void, _c_size]),

@@ -8,7 +8,9 @@ on a transfer stream as one transfer, and on a compute stream, as soon as its co
 records are decoded into PackedBatch tensors with their headers and payload CRC-32 checked on
 the GPU (ops.decode_records) and attended by the fused decode kernel. Reading chunk i + 1 on
 the host overlaps the GPU work of chunk i. The per-chunk (out, lse) pairs are merged exactly
-by one N-way merge kernel (the reference chains one pairwise merge per chunk), and the records'
+by one N-way merge kernel (the reference chains one pairwise merge per chunk). A store opened
+with the ``gds`` storage backend skips the pinned buffers and the copy: cuFile reads each chunk
+straight into one of two aligned device buffers. The records'
 integrity statuses are read back once at the end: a bad record raises as kvssd's decode_record
 does (ValueError for a bad header or layout, IOError for a CRC mismatch). For a layer that stays
 resident in HBM use DeviceBlockPool, which decodes with a single launch.
@@ -64,6 +66,14 @@ class KVSSDPipeline:
         self.transfer_stream = torch.cuda.Stream(device=self.device)
         self.compute_stream = torch.cuda.Stream(device=self.device)
         self._ring = [_PinnedChunk(store.spec, stage_blocks) for _ in range(2)]
+        # gds storage: records land in device memory by cuFile, no pinned staging or copy
+        self._device_ring = None
+        if store.reads_to_device:
+            from .storage import _aligned
+
+            rb = store.spec.record_bytes
+            self._device_ring = [_aligned(stage_blocks * rb, self.device) for _ in range(2)]
+            self._device_free = [None, None]  # event: the compute stream is done with a buffer
 
     def decode(self, query: torch.Tensor, layer: int,
                selector: BlockSelector | None = None) -> torch.Tensor:
@@ -87,18 +97,32 @@ class KVSSDPipeline:
 
         for ci in range(n_chunks):
             lo, hi = ci * self.stage_blocks, min(len(selected), (ci + 1) * self.stage_blocks)
-            chunk = self._ring[ci % len(self._ring)]
-            if chunk.copied is not None:
-                chunk.copied.synchronize()  # the pinned buffer's previous copy has landed
-            raw = self.store.read_records(layer, selected[lo:hi], destination=chunk.raw,
-                                          threads=self.io_depth)
-            with torch.cuda.stream(self.transfer_stream):
-                dev = raw.to(self.device, non_blocking=True)
-                chunk.copied = torch.cuda.Event()
-                chunk.copied.record(self.transfer_stream)
+            if self._device_ring is not None:
+                slot = ci % 2
+                if self._device_free[slot] is not None:
+                    self._device_free[slot].synchronize()  # its previous chunk is decoded
+                dev = self.store.read_records(layer, selected[lo:hi],
+                                              destination=self._device_ring[slot],
+                                              threads=self.io_depth)
+                ready = None
+            else:
+                chunk = self._ring[ci % len(self._ring)]
+                if chunk.copied is not None:
+                    chunk.copied.synchronize()  # the pinned buffer's previous copy has landed
+                raw = self.store.read_records(layer, selected[lo:hi], destination=chunk.raw,
+                                              threads=self.io_depth)
+                with torch.cuda.stream(self.transfer_stream):
+                    dev = raw.to(self.device, non_blocking=True)
+                    chunk.copied = torch.cuda.Event()
+                    chunk.copied.record(self.transfer_stream)
+                ready = chunk.copied
             with torch.cuda.stream(self.compute_stream):
-                self.compute_stream.wait_event(chunk.copied)
+                if ready is not None:
+                    self.compute_stream.wait_event(ready)
                 kp, vp, ks, vs, valid, status = ops.decode_records(dev, spec, layer, ids[lo:hi])
+                if self._device_ring is not None:
+                    self._device_free[ci % 2] = torch.cuda.Event()
+                    self._device_free[ci % 2].record(self.compute_stream)
                 self._attend(query, PackedBatch(kp, vp, ks, vs, valid, spec.bits,
                                                 spec.group_size), scale, outs[ci], lses[ci])
                 statuses[lo:hi].copy_(status)

@@ -1,9 +1,12 @@
 """KVCacheStore: append-only fixed-record KV cache file plus manifest.
 
 API-compatible with src/kvssd/store.py:20-113 (create / open / entry / blocks_for_layer /
-read_into / read / close) and byte-compatible on disk. Storage is positioned reads (pread)
-of whole 4 KiB-aligned records; the reference's O_DIRECT and cuFile storage backends are not
-part of this package.
+read_into / read / close) and byte-compatible on disk. Host reads are positioned reads (pread)
+of whole 4 KiB-aligned records, batched through the native O_DIRECT reader by read_records;
+with the ``gds`` storage backend (storage.py) read_records and read_into also take CUDA
+destinations, filled by cuFile straight from the file. The default (None) is ``buffered``
+(the native batch reader still tries O_DIRECT); ``auto`` follows kvssd's order (gds, direct,
+buffered).
 """
 
 from __future__ import annotations
@@ -81,13 +84,14 @@ class _PreadFile:
 class KVCacheStore:
     """Append-only fixed-record KV cache store designed for large sequential reads."""
 
-    def __init__(self, root: str | Path, manifest: Manifest, storage_backend: str | None = None):
-        if storage_backend not in (None, "auto", "buffered"):
-            raise ValueError(
-                f"storage backend '{storage_backend}' is not provided by kvssd_b200; "
-                "use 'buffered' (positioned reads)"
-            )
+    def __init__(self, root: str | Path, manifest: Manifest, storage_backend=None):
+        from .storage import resolve_storage_backend
+
         self.root = Path(root)
+        # None: positioned reads, batched by read_records through the native reader (which
+        # uses O_DIRECT where the file system allows it)
+        self.storage_backend = resolve_storage_backend(
+            "buffered" if storage_backend is None else storage_backend, self.root / DATA_FILE)
         self.manifest = manifest
         self.spec = manifest.spec
         self._entries = {(e.layer, e.block): e for e in manifest.entries}
@@ -161,7 +165,17 @@ class KVCacheStore:
         """Sorted block ids of a layer (precomputed; the reference scans all entries)."""
         return list(self._layer_blocks.get(layer, []))
 
+    @property
+    def reads_to_device(self) -> bool:
+        """True when read_records can fill CUDA destinations directly (the gds backend)."""
+        return getattr(self.storage_backend, "name", "") == "gds"
+
     def read_into(self, entry: BlockEntry, destination: torch.Tensor) -> None:
+        if destination.device.type == "cuda":
+            if not self.reads_to_device:
+                raise ValueError("CUDA destinations need the 'gds' storage backend")
+            self.storage_backend.read_into(entry, destination)
+            return
         self._file.read_into(entry, destination)
 
     def read_records(self, layer: int, block_ids, destination: torch.Tensor | None = None,
@@ -169,13 +183,27 @@ class KVCacheStore:
         """Raw records of ``block_ids`` in one call of the native reader (O_DIRECT where the file
         system allows it, a pool of reader threads). Returns uint8 [n, record_bytes] (pinned
         when CUDA is available, or ``destination``), ready for one host-to-device copy and
-        ops.decode_records on the GPU."""
+        ops.decode_records on the GPU. A CUDA ``destination`` (4096-byte aligned) is filled by
+        cuFile with the gds backend, with no host copy."""
         import ctypes
 
         from . import _native
 
         ids = list(block_ids)
         rb = self.spec.record_bytes
+        if destination is not None and destination.device.type == "cuda":
+            if not self.reads_to_device:
+                raise ValueError("CUDA destinations need the 'gds' storage backend")
+            offsets = []
+            for b in ids:
+                entry = self.entry(layer, b)
+                if entry.length != rb:
+                    raise ValueError("records of one store all have the spec's record_bytes")
+                offsets.append(entry.offset)
+            flat = destination.view(-1)
+            self.storage_backend.read_records(offsets, rb, flat, threads)
+            self.last_read_direct = True
+            return flat[: len(ids) * rb].view(len(ids), rb)
         if destination is None:
             destination = torch.empty((len(ids), rb), dtype=torch.uint8,
                                       pin_memory=torch.cuda.is_available())
@@ -208,6 +236,7 @@ class KVCacheStore:
 
     def close(self) -> None:
         self._file.close()
+        self.storage_backend.close()
 
     def __enter__(self) -> "KVCacheStore":
         return self

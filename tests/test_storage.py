@@ -1,0 +1,55 @@
+"""Storage backend selection with kvssd's storage API (src/kvssd/storage/registry.py:15-68):
+names, ``auto`` order, refusals, and the cuFile (gds) backend's probe reporting why it is
+unavailable on a host without a CUDA device. The gds read path itself is tested on the GPU
+(tests/test_gpu_gds.py)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from kvssd_b200 import (CacheSpec, GDSStorageBackend, KVCacheStore, available_storage_backends,
+                        resolve_storage_backend)
+from kvssd_b200.format import PackedKVBlock
+from kvssd_b200.quant import quantize_tensor
+from kvssd_b200.storage import BufferedStorageBackend
+
+
+def _store(tmp_path, **kw):
+    spec = CacheSpec(layers=1, kv_heads=2, head_dim=64, block_tokens=16, bits=4, group_size=32)
+    gen = torch.Generator().manual_seed(3)
+    blocks = []
+    for b in range(3):
+        x = torch.randn(2, 16, 2, 64, generator=gen).half()
+        blocks.append(PackedKVBlock(0, b, 16, quantize_tensor(x[0], 4, 32),
+                                    quantize_tensor(x[1], 4, 32)))
+    return KVCacheStore.from_blocks(tmp_path / "s", spec, blocks, **kw)
+
+
+def test_default_store_reads_with_positioned_reads(tmp_path):
+    store = _store(tmp_path)
+    assert isinstance(store.storage_backend, BufferedStorageBackend)
+    assert not store.reads_to_device
+    blk = store.read(0, 1)
+    assert blk.valid_tokens == 16
+    store.close()
+
+
+def test_unknown_and_unavailable_backends_are_refused(tmp_path):
+    store = _store(tmp_path)
+    path = store.root / "blocks.kvssd"
+    with pytest.raises(ValueError, match="unknown storage backend 'nvme'"):
+        resolve_storage_backend("nvme", path)
+    if not torch.cuda.is_available():
+        state = GDSStorageBackend(path).probe()
+        assert not state.available and "CUDA" in state.reason
+        with pytest.raises(RuntimeError, match="storage backend 'gds' unavailable"):
+            KVCacheStore.open(store.root, storage_backend="gds")
+    names = [s.name for s in available_storage_backends(path)]
+    assert names[:3] == ["gds", "direct", "buffered"]
+    auto = resolve_storage_backend("auto", path)  # gds, else direct, else buffered
+    assert auto.probe().available
+    assert resolve_storage_backend(None, path).name in ("gds", "direct", "buffered")
+    missing = tmp_path / "nothing.kvssd"
+    assert not BufferedStorageBackend(missing).probe().available
+    store.close()
