@@ -67,6 +67,9 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target duration of the CPU-baseline sample")
     ap.add_argument("--no-c4", action="store_true", help="skip the c4 multi-layer leg")
+    ap.add_argument("--records-only", action="store_true",
+                    help="profiling aid: only the on-GPU record decode of the c2 layer's 1024 "
+                         "records (one JSON line with its timing)")
     return ap.parse_args()
 
 
@@ -275,6 +278,53 @@ def pipeline_legs(w, base, q, scale, device, rank, args) -> dict:
             "note": "1024 raw records resident in HBM -> PackedBatch + CRC-32 check (reads the "
                     "records, writes the packed KV: hbm_frac counts both)"},
     }
+
+
+def records_only(args) -> None:
+    """The record-decode leg alone: the c2 layer written as a store in /dev/shm, its 1024 raw
+    records read into HBM, then ``args.warmup`` + ``args.steps`` ops.decode_records calls (the
+    timed ones between CUDA events on the current stream)."""
+    from kvssd_b200 import CacheSpec, KVCacheStore, ops
+    from kvssd_b200.format import PackedKVBlock
+    from kvssd_b200.quant import QuantizedTensor
+    from kvssd_b200.workloads import WORKLOADS, make_layer
+
+    device = torch.device("cuda", 0)
+    w = WORKLOADS[WORKLOAD]
+    lay = make_layer(w, 0, "cpu")
+    spec = CacheSpec(1, w.kv_heads, w.head_dim, w.block_tokens, w.bits, w.group_size)
+    shape = (w.block_tokens, w.kv_heads, w.head_dim)
+    blocks = (PackedKVBlock(0, b, int(lay.valid_tokens[b]),
+                            QuantizedTensor(lay.packed_k[b], lay.scales_k[b], shape, w.bits,
+                                            w.group_size),
+                            QuantizedTensor(lay.packed_v[b], lay.scales_v[b], shape, w.bits,
+                                            w.group_size))
+              for b in range(lay.packed_k.shape[0]))
+    root = Path(tempfile.mkdtemp(prefix="kvssd_records_", dir="/dev/shm"
+                                 if Path("/dev/shm").is_dir() else None))
+    try:
+        store = KVCacheStore.from_blocks(root, spec, blocks)
+        raw = store.read_records(0, store.blocks_for_layer(0)).to(device)
+        store.close()
+        for _ in range(max(3, args.warmup)):
+            out = ops.decode_records(raw, spec, 0)
+        torch.cuda.synchronize(device)
+        if int((out[5] != 0).sum()) or not torch.equal(out[0].cpu(), lay.packed_k):
+            raise BenchFailure("record decode does not reproduce the layer")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            ops.decode_records(raw, spec, 0)
+        e1.record()
+        torch.cuda.synchronize(device)
+        us = e0.elapsed_time(e1) / args.steps * 1e3
+    finally:
+        shutil.rmtree(root, ignore_errors=True)
+    moved = raw.numel() + w.blocks_per_layer * w.bytes_per_block
+    emit({"records_only": {"us_per_layer": us, "hbm_bytes_per_layer": moved,
+                           "GB/s": moved / (us * 1e-6) / 1e9,
+                           "hbm_frac": moved / (us * 1e-6) / 1e9 / peaks()[0],
+                           "steps": args.steps, "warmup": max(3, args.warmup)}})
 
 
 def graph_time(fn, device, reps: int = 20, rotate: int = 1) -> float:
@@ -773,6 +823,9 @@ def main() -> None:
         run_reference(args)
         return
     try:
+        if args.records_only:
+            records_only(args)
+            return
         run_ours(args)
     except Exception as exc:  # a failed check prints no result line and exits non-zero
         from kvssd_b200.ops import DeviceFailure
