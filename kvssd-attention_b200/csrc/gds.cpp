@@ -4,7 +4,9 @@
 // libcufile is loaded at run time (dlopen), so the library itself has no link dependency on it
 // and reports KVSSD_B200_ERR_UNSUPPORTED, with the reason, where cuFile cannot be used. The
 // driver is opened once per process on first use and left open. A batch of records is read by
-// a pool of threads, one cuFileRead per record (cuFile calls are thread safe). Host code only.
+// a pool of threads on the caller's device, one cuFileRead per record (cuFile calls are thread
+// safe). Host code: no kernels.
+#include <cuda_runtime.h>
 #include <cufile.h>
 #include <dlfcn.h>
 #include <errno.h>
@@ -144,12 +146,16 @@ int kvssd_b200_gds_read_records(kvssd_b200_gds_file* file, const long long* offs
   const CuFileApi& api = cufile();
   if (!api.error.empty()) return fail(KVSSD_B200_ERR_UNSUPPORTED, api.error);
   const int n_threads = std::max(1, std::min(threads, n_records));
+  int device = 0;  // the reader threads work on the caller's device
+  if (cudaGetDevice(&device) != cudaSuccess)
+    return fail(KVSSD_B200_ERR_CUDA, "cudaGetDevice failed");
   std::atomic<int> next{0};
   std::atomic<bool> failed{false};
   std::mutex err_mu;
   std::string first_error;
   auto worker = [&] {
     std::string err;
+    cudaSetDevice(device);
     for (int i = next++; i < n_records && !failed.load(); i = next++) {
       if (!read_record(api, file, device_destination, record_bytes, offsets[i],
                        static_cast<long long>(i) * static_cast<long long>(record_bytes), &err)) {
