@@ -87,6 +87,15 @@ def test_refused_descriptor_is_flagged_and_others_decode():
     ref_out, _ = ops.decode(q, *good, 4, 32, SCALE)
     torch.testing.assert_close(outs[0][0], ref_out, **NEAR)
     torch.testing.assert_close(outs[2][0], ref_out, **NEAR)
+    # The refused problem's combining CTAs still count themselves, so the grid's epoch moves
+    # on: later calls read this call's parts, not the previous call's (new query each time).
+    for _ in range(2):
+        q.neg_()
+        outs = batch.run()
+        torch.cuda.synchronize()
+        ref_out, _ = ops.decode(q, *good, 4, 32, SCALE)
+        torch.testing.assert_close(outs[0][0], ref_out, **NEAR)
+        torch.testing.assert_close(outs[2][0], ref_out, **NEAR)
 
 
 def test_batched_refuses_other_shapes():
