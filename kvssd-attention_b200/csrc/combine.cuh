@@ -168,6 +168,11 @@ __device__ __forceinline__ void combine_slice_warp(const float* __restrict__ par
 // epoch is the call number kept in the workspace header: every CTA reads the previous call's
 // at its start, and the combiners store this call's after their fold (they have seen every
 // CTA's part, so every CTA of the call has read the header by then).
+// What a tag cannot tell apart: a word left by a call 2^31 - 1 calls earlier (the epoch wraps)
+// that no call has rewritten since, and plain f32 parts written over the region by the
+// separate-combine path, whose high halves are f32 bit patterns (a positive one equal to a
+// small epoch is a denormal near 1e-44). Zeroing the workspace at allocation rules out
+// leftover garbage.
 constexpr unsigned kTagPoison = 0x80000000u;
 
 __device__ __forceinline__ unsigned next_epoch(unsigned prev) {
