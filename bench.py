@@ -236,7 +236,8 @@ def pipeline_legs(w, base, q, scale, device, rank, args) -> dict:
     store = KVCacheStore.from_blocks(root, spec, blocks)
     record_bytes = kp.shape[0] * spec.record_bytes
     try:
-        pipe = KVSSDPipeline(store, device=device, io_depth=8, stage_blocks=128,
+        io_depth = max(1, min(16, os.cpu_count() or 1))  # one reader thread per core, <= 16
+        pipe = KVSSDPipeline(store, device=device, io_depth=io_depth, stage_blocks=128,
                              require_cuda_kernel=True)
         qh = q.float()
         for _ in range(2):
@@ -267,7 +268,7 @@ def pipeline_legs(w, base, q, scale, device, rank, args) -> dict:
     return {
         "KVSSDPipeline_decode": {
             "value": nbytes / pipe_s / 1e9, "unit": "GB/s", "ms_per_step": pipe_s * 1e3,
-            "path": "KVSSDPipeline(store, stage_blocks=128, io_depth=8).decode(query, 0): "
+            "path": f"KVSSDPipeline(store, stage_blocks=128, io_depth={io_depth}).decode(query, 0): "
                     "store file in /dev/shm (page cache), native record reads, H2D, on-GPU "
                     "record decode with CRC-32, fused decode, chunk merge; host wall clock"},
         "record_decode_on_gpu": {
