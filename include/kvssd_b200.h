@@ -172,8 +172,13 @@ KVSSD_B200_API int kvssd_b200_set_path_override(int path);
  * device; record_status[i] receives the OR of 1 = bad magic/version, 2 = geometry differs from
  * the arguments, 4 = payload length differs, 8 = CRC mismatch, 16 = layer/block differs from
  * `layer` (if >= 0) / expected_blocks[i] (if not NULL), 32 = valid count above block_tokens
- * (clamped). Records with status bits 1, 2 or 4 are not copied and get valid 0. Replaces the
- * CPU decode_record of the reference loader (src/kvssd/format.py:134-177,
+ * (clamped). Records with status bits 1, 2 or 4 are not copied and get valid 0. Asynchronous on
+ * `stream`. With 16-byte aligned records, stride and outputs and both section sizes
+ * (bt*kvh*(d/group)*2 and bt*kvh*d*bits/8 bytes) multiples of 16, as in the c1-c5 geometries,
+ * one streaming kernel does the copy and the CRC in a single pass, after a small kernel that zeroes
+ * record_status and valid_tokens (they hold the per-record CRC partials and row counts until
+ * the last contribution writes the final values); other inputs take a per-record kernel.
+ * Replaces the CPU decode_record of the reference loader (src/kvssd/format.py:134-177,
  * src/kvssd/loader.py:104-128), which checks the CRC on the host. */
 KVSSD_B200_API int kvssd_b200_decode_records(const uint8_t* records, size_t record_stride,
                       int n_records, int layer, const int32_t* expected_blocks, int bits,
