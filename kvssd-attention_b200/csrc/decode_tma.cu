@@ -213,9 +213,11 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP, BITS>::THREADS, 1)
       const int ld_row = lane & 7, ld_chunk = lane >> 3;
       const uint32_t ld_off =
           static_cast<uint32_t>(ld_row * 64 + ((ld_chunk ^ ((ld_row >> 1) & 3)) << 4));
-      // Unrolled by the ring depth: stage index, parity and addresses fold to constants
-      // (measured: c2 decode 40.6 -> 37.7 us; INT2 128K 39.6 -> 38.3 us split).
-#pragma unroll 4
+      // Unrolled by twice the ring depth: stage index, parity and addresses fold to constants
+      // (measured, c2 decode: no unroll 40.6 us, 2: 38.8, 4: 37.6, 8: 37.3, 16: 41.5). Group 64
+      // keeps 4: its scale handling needs more registers, and 8 spills there.
+      constexpr int kUnroll = GROUP == 32 ? 8 : 4;
+#pragma unroll kUnroll
       for (int i = 0; i < n_mine; ++i) {
         const int sl = grp * kTmaSlots + i % kTmaSlots;
         if (!wait_stage(i, sl)) break;
@@ -242,7 +244,7 @@ __global__ void __launch_bounds__(TmaLayout<KVH, 128 / GROUP, BITS>::THREADS, 1)
       QueryFrags2<GROUP> qfr;
       qfr.load(a, qsrc, q0, nq, g, c);
       const uint32_t ld_off = ld_off_int2(lane);
-#pragma unroll 4
+#pragma unroll (GROUP == 32 ? 8 : 4)
       for (int i = 0; i < n_mine; ++i) {
         const int sl = grp * kTmaSlots + i % kTmaSlots;
         if (!wait_stage(i, sl)) break;
