@@ -8,7 +8,10 @@
 // followed by the payload -- K scales, V scales (FP16, [bt, kvh, G] each), K codes, V codes
 // (u8, [bt, kvh, pd] each) -- and zero padding to a 4 KiB multiple.
 //
-// One CTA per record. Pass 1 copies the payload's four sections into their PackedBatch tensors
+// Two kernels. The streaming one (record_stream_kernel, below) takes every input whose
+// buffers are 16-byte aligned and whose sections are whole 16-byte units: one pass over the
+// records, copy and CRC together. The per-record kernel (record_decode_kernel) takes the rest:
+// one CTA per record. Pass 1 copies the payload's four sections into their PackedBatch tensors
 // with coalesced 4-byte words (the payload starts 4-byte aligned; geometries whose sections
 // are not whole words are copied byte by byte). Pass 2 checks the CRC: the
 // payload is cut into NT equal slices, thread t runs the table-driven reflected CRC-32 over
