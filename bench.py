@@ -249,6 +249,31 @@ def pipeline_legs(w, base, q, scale, device, rank, args) -> dict:
             out = pipe.decode(qh, 0)
             out.cpu()
         pipe_s = (time.perf_counter() - t0) / steps
+        ref_out = out.clone()
+        pipe.close()
+        # the same store opened with the "mapped" backend: page-locked mapping, DMA copies
+        mapped_s, mapped_note = None, None
+        try:
+            mstore = KVCacheStore.open(root, storage_backend="mapped")
+        except RuntimeError as exc:  # the driver would not page-lock the mapping
+            mapped_note = str(exc)
+        else:
+            try:
+                mpipe = KVSSDPipeline(mstore, device=device, stage_blocks=128,
+                                      require_cuda_kernel=True)
+                for _ in range(2):
+                    mout = mpipe.decode(qh, 0)
+                torch.cuda.synchronize(device)
+                if not torch.equal(mout, ref_out):
+                    raise BenchFailure("the mapped-store pipeline differs from the default one")
+                t0 = time.perf_counter()
+                for _ in range(steps):
+                    mout = mpipe.decode(qh, 0)
+                    mout.cpu()
+                mapped_s = (time.perf_counter() - t0) / steps
+                mpipe.close()
+            finally:
+                mstore.close()
         raw = store.read_records(0, store.blocks_for_layer(0)).to(device)
         for _ in range(3):
             ops.decode_records(raw, spec, 0)
@@ -260,7 +285,6 @@ def pipeline_legs(w, base, q, scale, device, rank, args) -> dict:
         e1.record()
         torch.cuda.synchronize(device)
         rec_ms = e0.elapsed_time(e1) / 10
-        pipe.close()
     finally:
         store.close()
         shutil.rmtree(root, ignore_errors=True)
@@ -271,6 +295,12 @@ def pipeline_legs(w, base, q, scale, device, rank, args) -> dict:
             "path": f"KVSSDPipeline(store, stage_blocks=128, io_depth={io_depth}).decode(query, 0): "
                     "store file in /dev/shm (page cache), native record reads, H2D, on-GPU "
                     "record decode with CRC-32, fused decode, chunk merge; host wall clock"},
+        "KVSSDPipeline_decode_mapped": (
+            {"value": nbytes / mapped_s / 1e9, "unit": "GB/s", "ms_per_step": mapped_s * 1e3,
+             "path": "the same store opened with storage_backend='mapped' (file mapped "
+                     "read-only and page-locked; records copied to the device by DMA, one "
+                     "copy per run of records), same pipeline; host wall clock"}
+            if mapped_s is not None else {"unavailable": mapped_note}),
         "record_decode_on_gpu": {
             "value": record_bytes / (rec_ms * 1e-3) / 1e9, "unit": "GB/s of records",
             "us_per_layer": rec_ms * 1e3,

@@ -212,6 +212,25 @@ KVSSD_B200_API const char* kvssd_b200_io_last_error(void);
  * `threads` reader threads; synchronous (the data is in device memory on return). Errors:
  * KVSSD_B200_ERR_INVALID_ARGUMENT for misaligned requests, KVSSD_B200_ERR_CUDA for a failed or
  * short cuFileRead (the reference raises OSError / EOFError). */
+/* Page-locked store files (the "mapped" storage backend): host_register registers a host
+ * range -- a store file mapped read-only with mmap, read_only = 1 -- with the CUDA driver
+ * (cudaHostRegister, portable; read-only where asked), and copy_records_h2d then copies
+ * n_records records of record_bytes at byte offsets of that range into device_destination +
+ * i * record_bytes on `stream`, asynchronously, one cudaMemcpyAsync per run of records that are
+ * consecutive in the file: the records travel by DMA from the page cache, with no reader
+ * threads and no staging copy (the reference reads them into a host buffer first,
+ * src/kvssd/storage/buffered.py:53-76, src/kvssd/pipeline.py:118-165). Offsets outside
+ * [0, host_bytes) are refused (KVSSD_B200_ERR_INVALID_ARGUMENT) before anything is copied;
+ * a range the driver will not register gives KVSSD_B200_ERR_UNSUPPORTED with the reason in
+ * kvssd_b200_host_last_error. */
+KVSSD_B200_API int kvssd_b200_host_register(void* ptr, size_t bytes, int read_only);
+KVSSD_B200_API int kvssd_b200_host_unregister(void* ptr);
+KVSSD_B200_API int kvssd_b200_copy_records_h2d(const void* host_base, size_t host_bytes,
+                                               const long long* offsets, int n_records,
+                                               size_t record_bytes, void* device_destination,
+                                               kvssd_b200_stream_t stream);
+KVSSD_B200_API const char* kvssd_b200_host_last_error(void);
+
 typedef struct kvssd_b200_gds_file kvssd_b200_gds_file;
 KVSSD_B200_API int kvssd_b200_gds_open(const char* path, kvssd_b200_gds_file** file);
 KVSSD_B200_API int kvssd_b200_gds_read_records(kvssd_b200_gds_file* file,

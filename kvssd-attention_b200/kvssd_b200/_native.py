@@ -96,6 +96,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          ctypes.POINTER(_c_int)],
     ),
     "kvssd_b200_io_last_error": (ctypes.c_char_p, []),
+    "kvssd_b200_host_register": (_c_int, [_c_void, _c_size, _c_int]),
+    "kvssd_b200_host_unregister": (_c_int, [_c_void]),
+    "kvssd_b200_copy_records_h2d": (_c_int, [_c_void, _c_size, _c_void, _c_int, _c_size, _c_void,
+                                             _c_void]),
+    "kvssd_b200_host_last_error": (ctypes.c_char_p, []),
     "kvssd_b200_gds_open": (_c_int, [ctypes.c_char_p, ctypes.POINTER(_c_void)]),
     "kvssd_b200_gds_read_records": (_c_int, [_c_void, _c_void, _c_int, _c_size, _c_void, _c_int]),
     "kvssd_b200_gds_close": (_c_int, [_c_void]),

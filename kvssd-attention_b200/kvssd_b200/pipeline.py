@@ -10,7 +10,8 @@ the GPU (ops.decode_records) and attended by the fused decode kernel. Reading ch
 the host overlaps the GPU work of chunk i. The per-chunk (out, lse) pairs are merged exactly
 by one N-way merge kernel (the reference chains one pairwise merge per chunk). A store opened
 with the ``gds`` storage backend skips the pinned buffers and the copy: cuFile reads each chunk
-straight into one of two aligned device buffers. The records'
+straight into one of two aligned device buffers, and one opened with ``mapped`` copies the
+records into them by DMA from the page-locked file mapping on the transfer stream. The records'
 integrity statuses are read back once at the end: a bad record raises as kvssd's decode_record
 does (ValueError for a bad header or layout, IOError for a CRC mismatch). For a layer that stays
 resident in HBM use DeviceBlockPool, which decodes with a single launch.
@@ -66,7 +67,8 @@ class KVSSDPipeline:
         self.transfer_stream = torch.cuda.Stream(device=self.device)
         self.compute_stream = torch.cuda.Stream(device=self.device)
         self._ring = [_PinnedChunk(store.spec, stage_blocks) for _ in range(2)]
-        # gds storage: records land in device memory by cuFile, no pinned staging or copy
+        # gds / mapped storage: records land in device memory by cuFile or by DMA from the
+        # page-locked file mapping, with no pinned staging buffer
         self._device_ring = None
         if store.reads_to_device:
             from .storage import _aligned
@@ -99,12 +101,23 @@ class KVSSDPipeline:
             lo, hi = ci * self.stage_blocks, min(len(selected), (ci + 1) * self.stage_blocks)
             if self._device_ring is not None:
                 slot = ci % 2
-                if self._device_free[slot] is not None:
-                    self._device_free[slot].synchronize()  # its previous chunk is decoded
-                dev = self.store.read_records(layer, selected[lo:hi],
-                                              destination=self._device_ring[slot],
-                                              threads=self.io_depth)
-                ready = None
+                if getattr(self.store.storage_backend, "device_reads_async", False):
+                    # mapped: DMA copies on the transfer stream, after the slot's last decode
+                    with torch.cuda.stream(self.transfer_stream):
+                        if self._device_free[slot] is not None:
+                            self.transfer_stream.wait_event(self._device_free[slot])
+                        dev = self.store.read_records(layer, selected[lo:hi],
+                                                      destination=self._device_ring[slot])
+                        ready = torch.cuda.Event()
+                        ready.record(self.transfer_stream)
+                else:
+                    # gds: cuFile writes device memory from the host thread, synchronously
+                    if self._device_free[slot] is not None:
+                        self._device_free[slot].synchronize()  # its previous chunk is decoded
+                    dev = self.store.read_records(layer, selected[lo:hi],
+                                                  destination=self._device_ring[slot],
+                                                  threads=self.io_depth)
+                    ready = None
             else:
                 chunk = self._ring[ci % len(self._ring)]
                 if chunk.copied is not None:

@@ -237,8 +237,146 @@ class GDSStorageBackend:
                 self._file = None
 
 
+class MappedStorageBackend:
+    """The store file mapped (mmap) and page-locked with the CUDA driver: reads into
+    CUDA destinations are asynchronous DMA copies from the page cache on the current stream
+    (kvssd_b200_copy_records_h2d: one copy per run of consecutive records), with no reader
+    threads and no staging buffer; host reads are plain slices of the mapping. The whole file
+    stays pinned while the backend is open, so this is for stores that fit in host memory, and
+    one mapped backend per file at a time (the driver refuses to register the same pages
+    twice). Not in kvssd; opt-in by name (``auto`` does not pick it)."""
+
+    name = "mapped"
+    direct = False
+    device_reads_async = True
+
+    def __init__(self, path: str | Path):
+        self.path = Path(path)
+        self._map = None
+        self._view = None
+        self._registered = 0
+        self._lock = threading.Lock()
+
+    def _lib(self):
+        from . import _native
+
+        return _native.library()
+
+    def _mapping(self):
+        """(numpy view of the whole file, its address), mapping and registering on first use."""
+        import mmap
+
+        import numpy as np
+
+        with self._lock:
+            if self._view is None:
+                size = self.path.stat().st_size
+                if size == 0:
+                    raise OSError(f"empty data file: {self.path}")
+                lib = self._lib()
+                reasons = []
+                # A shared read-only mapping registered read-only pins the page cache itself;
+                # where the driver refuses that, a private mapping registered for writing
+                # pins private copies of the pages (made once, at registration).
+                for flags, prot, read_only in ((mmap.MAP_SHARED, mmap.PROT_READ, 1),
+                                               (mmap.MAP_PRIVATE,
+                                                mmap.PROT_READ | mmap.PROT_WRITE, 0)):
+                    with open(self.path, "rb") as f:
+                        mm = mmap.mmap(f.fileno(), size, flags=flags, prot=prot)
+                    view = np.frombuffer(mm, dtype=np.uint8)
+                    addr = view.ctypes.data
+                    if lib.kvssd_b200_host_register(addr, size, read_only) == 0:
+                        self._map, self._view, self._registered = mm, view, addr
+                        break
+                    reasons.append(lib.kvssd_b200_host_last_error().decode())
+                    del view
+                    mm.close()
+                else:
+                    raise OSError("; ".join(reasons))
+            return self._view, self._registered
+
+    def probe(self) -> StorageAvailability:
+        def no(reason: str) -> StorageAvailability:
+            return StorageAvailability(self.name, False, False, True, reason)
+
+        if not self.path.is_file():
+            return no(f"data file does not exist: {self.path}")
+        if not torch.cuda.is_available():
+            return no("page-locking a mapped file requires a CUDA device")
+        # Map, register and let go again: the driver refuses a second registration of the same
+        # pages, so a probe (available_storage_backends probes and drops every backend) must not
+        # keep them; the first read maps the file anew.
+        was_open = self._view is not None
+        try:
+            self._mapping()
+        except Exception as exc:  # mmap refused, or the driver would not register the range
+            return no(f"mapping failed: {exc}")
+        finally:
+            if not was_open:
+                self.close()
+        return StorageAvailability(self.name, True, False, True,
+                                   "page-locked file mapping; DMA copies to the device")
+
+    def allocate_buffer(self, size: int, *, pinned: bool = False,
+                        device: torch.device | None = None) -> torch.Tensor:
+        del pinned
+        return _aligned(size, device or torch.device("cuda"))
+
+    def read_records(self, offsets: list[int], record_bytes: int, destination: torch.Tensor,
+                     threads: int = 8) -> None:
+        """Records at ``offsets`` into destination[i * record_bytes:] (a CUDA uint8 tensor),
+        enqueued on the current stream of the destination's device."""
+        del threads
+        if destination.device.type != "cuda" or destination.dtype != torch.uint8:
+            raise ValueError("mapped reads into the device need a CUDA uint8 destination")
+        if not destination.is_contiguous() or destination.numel() < len(offsets) * record_bytes:
+            raise ValueError("destination must be contiguous and large enough")
+        if not offsets:
+            return
+        view, addr = self._mapping()
+        arr = (ctypes.c_longlong * len(offsets))(*offsets)
+        lib = self._lib()
+        stream = torch.cuda.current_stream(destination.device).cuda_stream
+        with torch.cuda.device(destination.device):
+            st = lib.kvssd_b200_copy_records_h2d(addr, view.size, arr, len(offsets), record_bytes,
+                                                 destination.data_ptr(), stream)
+        if st != 0:
+            raise OSError(f"mapped record copy failed: {lib.kvssd_b200_host_last_error().decode()}")
+
+    def read_into(self, entry: BlockEntry, destination: torch.Tensor) -> None:
+        if destination.device.type == "cuda":
+            self.read_records([entry.offset], entry.length, destination)
+            return
+        if destination.dtype != torch.uint8 or destination.numel() < entry.length:
+            raise ValueError("destination must be a sufficiently large uint8 tensor")
+        view, _ = self._mapping()
+        if entry.offset + entry.length > view.size:
+            raise EOFError(f"short read for layer={entry.layer}, block={entry.block}")
+        destination[: entry.length].copy_(
+            torch.from_numpy(view[entry.offset:entry.offset + entry.length].copy()))
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def close(self) -> None:
+        with self._lock:
+            if self._view is not None:
+                try:
+                    torch.cuda.synchronize()  # no copy from the mapping may still be in flight
+                except Exception:
+                    pass
+                self._lib().kvssd_b200_host_unregister(self._registered)
+                self._view = None
+                self._map.close()
+                self._map = None
+                self._registered = 0
+
+
 _FACTORIES = {"gds": GDSStorageBackend, "direct": DirectStorageBackend,
-              "buffered": BufferedStorageBackend}
+              "buffered": BufferedStorageBackend, "mapped": MappedStorageBackend}
 
 
 def register_storage_backend(name: str, factory) -> None:
@@ -264,7 +402,7 @@ def resolve_storage_backend(requested, path: str | Path):
         return requested
     key = (requested or "auto").strip().lower()
     if key == "auto":
-        for name in ("gds", "direct", "buffered"):
+        for name in ("gds", "direct", "buffered"):  # not "mapped": it pins the whole file
             backend = _FACTORIES[name](path)
             if backend.probe().available:
                 return backend

@@ -4,7 +4,8 @@ API-compatible with src/kvssd/store.py:20-113 (create / open / entry / blocks_fo
 read_into / read / close) and byte-compatible on disk. Host reads are positioned reads (pread)
 of whole 4 KiB-aligned records, batched through the native O_DIRECT reader by read_records;
 with the ``gds`` storage backend (storage.py) read_records and read_into also take CUDA
-destinations, filled by cuFile straight from the file. The default (None) is ``buffered``
+destinations, filled by cuFile straight from the file, and with ``mapped`` (the file mapped and
+page-locked) by DMA copies from the page cache. The default (None) is ``buffered``
 (the native batch reader still tries O_DIRECT); ``auto`` follows kvssd's order (gds, direct,
 buffered).
 """
@@ -167,13 +168,14 @@ class KVCacheStore:
 
     @property
     def reads_to_device(self) -> bool:
-        """True when read_records can fill CUDA destinations directly (the gds backend)."""
-        return getattr(self.storage_backend, "name", "") == "gds"
+        """True when read_records can fill CUDA destinations directly: cuFile (gds, synchronous)
+        or DMA from the page-locked mapping (mapped, enqueued on the current stream)."""
+        return getattr(self.storage_backend, "name", "") in ("gds", "mapped")
 
     def read_into(self, entry: BlockEntry, destination: torch.Tensor) -> None:
         if destination.device.type == "cuda":
             if not self.reads_to_device:
-                raise ValueError("CUDA destinations need the 'gds' storage backend")
+                raise ValueError("CUDA destinations need the 'gds' or 'mapped' storage backend")
             self.storage_backend.read_into(entry, destination)
             return
         self._file.read_into(entry, destination)
@@ -193,7 +195,7 @@ class KVCacheStore:
         rb = self.spec.record_bytes
         if destination is not None and destination.device.type == "cuda":
             if not self.reads_to_device:
-                raise ValueError("CUDA destinations need the 'gds' storage backend")
+                raise ValueError("CUDA destinations need the 'gds' or 'mapped' storage backend")
             offsets = []
             for b in ids:
                 entry = self.entry(layer, b)
@@ -202,7 +204,7 @@ class KVCacheStore:
                 offsets.append(entry.offset)
             flat = destination.view(-1)
             self.storage_backend.read_records(offsets, rb, flat, threads)
-            self.last_read_direct = True
+            self.last_read_direct = bool(self.storage_backend.direct)
             return flat[: len(ids) * rb].view(len(ids), rb)
         if destination is None:
             destination = torch.empty((len(ids), rb), dtype=torch.uint8,
