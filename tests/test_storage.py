@@ -53,3 +53,29 @@ def test_unknown_and_unavailable_backends_are_refused(tmp_path):
     missing = tmp_path / "nothing.kvssd"
     assert not BufferedStorageBackend(missing).probe().available
     store.close()
+
+
+def test_mapped_backend_and_record_copy_refusals_without_a_gpu(tmp_path):
+    """The mapped backend reports why it is unavailable, and the C ABI refuses out-of-range
+    record copies before it touches CUDA (no device is needed for either)."""
+    import ctypes
+
+    from kvssd_b200 import _native
+    from kvssd_b200.storage import MappedStorageBackend
+
+    store = _store(tmp_path)
+    path = store.root / "blocks.kvssd"
+    if not torch.cuda.is_available():
+        state = MappedStorageBackend(path).probe()
+        assert not state.available and "CUDA" in state.reason
+    assert "mapped" in [s.name for s in available_storage_backends(path)]
+    assert resolve_storage_backend("auto", path).name != "mapped"  # opt-in only
+    lib = _native.library()
+    host = (ctypes.c_uint8 * 8192)()
+    offsets = (ctypes.c_longlong * 2)(0, 8192)  # the second record runs past the range
+    st = lib.kvssd_b200_copy_records_h2d(ctypes.addressof(host), 8192, offsets, 2, 4096,
+                                         ctypes.addressof(host), None)
+    assert st == _native.ERR_INVALID_ARGUMENT
+    assert "outside the mapped range" in lib.kvssd_b200_host_last_error().decode()
+    assert lib.kvssd_b200_host_register(None, 0, 1) == _native.ERR_INVALID_ARGUMENT
+    store.close()
