@@ -255,6 +255,7 @@ class MappedStorageBackend:
         self._map = None
         self._view = None
         self._registered = 0
+        self._devices: set[int] = set()  # devices with copies from the mapping enqueued
         self._lock = threading.Lock()
 
     def _lib(self):
@@ -337,6 +338,8 @@ class MappedStorageBackend:
         arr = (ctypes.c_longlong * len(offsets))(*offsets)
         lib = self._lib()
         stream = torch.cuda.current_stream(destination.device).cuda_stream
+        with self._lock:
+            self._devices.add(destination.device.index)
         with torch.cuda.device(destination.device):
             st = lib.kvssd_b200_copy_records_h2d(addr, view.size, arr, len(offsets), record_bytes,
                                                  destination.data_ptr(), stream)
@@ -364,10 +367,13 @@ class MappedStorageBackend:
     def close(self) -> None:
         with self._lock:
             if self._view is not None:
-                try:
-                    torch.cuda.synchronize()  # no copy from the mapping may still be in flight
-                except Exception:
-                    pass
+                # no copy from the mapping may still be in flight, on any device it fed
+                for device in sorted(self._devices):
+                    try:
+                        torch.cuda.synchronize(device)
+                    except Exception:
+                        pass
+                self._devices.clear()
                 self._lib().kvssd_b200_host_unregister(self._registered)
                 self._view = None
                 self._map.close()
@@ -386,8 +392,23 @@ def register_storage_backend(name: str, factory) -> None:
     _FACTORIES[key] = factory
 
 
+def _close(backend) -> None:
+    close = getattr(backend, "close", None)
+    if close is not None:
+        close()
+
+
 def available_storage_backends(path: str | Path) -> list[StorageAvailability]:
-    return [factory(Path(path)).probe() for factory in _FACTORIES.values()]
+    """The probe result of every registered backend for ``path``; each probed instance is closed
+    again (a gds probe opens a cuFile handle and an O_DIRECT descriptor)."""
+    states = []
+    for factory in _FACTORIES.values():
+        backend = factory(Path(path))
+        try:
+            states.append(backend.probe())
+        finally:
+            _close(backend)
+    return states
 
 
 def resolve_storage_backend(requested, path: str | Path):
@@ -406,7 +427,7 @@ def resolve_storage_backend(requested, path: str | Path):
             backend = _FACTORIES[name](path)
             if backend.probe().available:
                 return backend
-            backend.close() if hasattr(backend, "close") else None
+            _close(backend)
         raise RuntimeError(f"no storage backend is available for {path}")
     if key not in _FACTORIES:
         listed = ", ".join(["auto", *_FACTORIES])

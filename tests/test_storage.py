@@ -79,3 +79,35 @@ def test_mapped_backend_and_record_copy_refusals_without_a_gpu(tmp_path):
     assert "outside the mapped range" in lib.kvssd_b200_host_last_error().decode()
     assert lib.kvssd_b200_host_register(None, 0, 1) == _native.ERR_INVALID_ARGUMENT
     store.close()
+
+
+def test_backend_probes_are_closed_again(tmp_path, monkeypatch):
+    """available_storage_backends and ``auto`` close every instance they probe and drop (a gds
+    probe holds a cuFile handle and an O_DIRECT descriptor until closed)."""
+    from kvssd_b200 import storage
+
+    closed = []
+
+    class Counting(BufferedStorageBackend):
+        def close(self) -> None:
+            closed.append(self.name)
+            super().close()
+
+    class Unavailable(Counting):
+        name = "gds"
+
+        def probe(self):
+            return storage.StorageAvailability(self.name, False, True, True, "test stand-in")
+
+    store = _store(tmp_path)
+    path = store.root / "blocks.kvssd"
+    factories = {"gds": Unavailable, "direct": Counting, "buffered": Counting}
+    monkeypatch.setattr(storage, "_FACTORIES", factories)
+    states = available_storage_backends(path)
+    assert [s.available for s in states] == [False, True, True]
+    assert closed == ["gds", "buffered", "buffered"]  # Counting's name is "buffered"
+    closed.clear()
+    chosen = resolve_storage_backend("auto", path)
+    assert closed == ["gds"] and chosen.probe().available  # the chosen one stays open
+    chosen.close()
+    store.close()
