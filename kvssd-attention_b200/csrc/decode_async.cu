@@ -96,13 +96,12 @@ struct WarpFeed {
 
 template <int KVH, int GROUP>
 __device__ __forceinline__ void async_decode_body(const DecodeArgs& a) {
-  constexpr int D = 128, BITS = 4, G = D / GROUP, MT = D / 16, DEPTH = kAsyncDepth;
+  constexpr int D = 128, BITS = 4, G = D / GROUP, DEPTH = kAsyncDepth;
   constexpr int PD = D * BITS / 8;            // 64 bytes of codes per (token, head)
   constexpr int SB = 2 * G;                   // scale bytes per (token, head)
   constexpr int OFF_V = 16 * PD, OFF_KS = 32 * PD, OFF_VS = OFF_KS + 16 * SB;
   constexpr int STAGE = ((OFF_VS + 16 * SB) + 127) / 128 * 128;
   constexpr int WPH = kAsyncWarps / KVH;
-  constexpr float kLazyMax = 8.f;  // rescale only when a score beats the running max by 2^8
   using Feed = WarpFeed<KVH, G>;
   static_assert(G == 4 || G == 2, "scale rows must be whole 4-byte words");
   static_assert(DEPTH <= 32, "partial-tile flags are one bit per stage");

@@ -315,19 +315,20 @@ __device__ __forceinline__ void softmax_pv_tile(float (&x)[4], int rows, int g, 
 template <int GROUP, bool VRAW>
 __device__ __forceinline__ void finish_stream(StreamState& s, int c) {
   constexpr int G = 128 / GROUP;
-  if (!VRAW) return;
+  if constexpr (VRAW) {
 #pragma unroll
-  for (int gi = 0; gi < G; ++gi) {
-    const float v = (gi & 1) ? s.vs[1] : s.vs[0];
-    const float s0 = 8.f * __shfl_sync(0xffffffffu, v, 4 * (2 * c) + (gi >> 1));
-    const float s1 = 8.f * __shfl_sync(0xffffffffu, v, 4 * (2 * c + 1) + (gi >> 1));
+    for (int gi = 0; gi < G; ++gi) {
+      const float v = (gi & 1) ? s.vs[1] : s.vs[0];
+      const float s0 = 8.f * __shfl_sync(0xffffffffu, v, 4 * (2 * c) + (gi >> 1));
+      const float s1 = 8.f * __shfl_sync(0xffffffffu, v, 4 * (2 * c + 1) + (gi >> 1));
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      if ((16 * k) / GROUP != gi) continue;  // M-tile k covers dims 16k .. 16k + 15
-      s.acc[k][0] = fmaf(s.acc[k][0], 16777216.f, -s0);
-      s.acc[k][1] = fmaf(s.acc[k][1], 16777216.f, -s1);
-      s.acc[k][2] = fmaf(s.acc[k][2], 1048576.f, -s0);
-      s.acc[k][3] = fmaf(s.acc[k][3], 1048576.f, -s1);
+      for (int k = 0; k < 8; ++k) {
+        if ((16 * k) / GROUP != gi) continue;  // M-tile k covers dims 16k .. 16k + 15
+        s.acc[k][0] = fmaf(s.acc[k][0], 16777216.f, -s0);
+        s.acc[k][1] = fmaf(s.acc[k][1], 16777216.f, -s1);
+        s.acc[k][2] = fmaf(s.acc[k][2], 1048576.f, -s0);
+        s.acc[k][3] = fmaf(s.acc[k][3], 1048576.f, -s1);
+      }
     }
   }
 }
