@@ -111,3 +111,19 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path: Path):
     with pytest.raises(RuntimeError, match="not built"):
         _native.library()
     assert not _native.available()
+
+
+def test_documented_ctypes_stub_binds():
+    """The ctypes binding that the integration guide gives kvssd maintainers loads this library,
+    and its workspace query and error text work as written (host-side calls only)."""
+    guide = (ROOT / "INTEGRATION.md").read_text()
+    stub = re.search(r"```python\n(import ctypes, torch\n.*?)```", guide, re.S).group(1)
+    stub = stub.replace('"/path/to/libkvssd_b200.so"', repr(str(_native.LIB_PATH)))
+    scope: dict = {}
+    exec(compile(stub, "INTEGRATION.md", "exec"), scope)
+    lib = scope["_lib"]
+    need = ctypes.c_size_t()  # a geometry refused before the query reaches the device
+    assert lib.kvssd_b200_decode_workspace_size(1, 8, 4, 2, 32, 3, 16,
+                                                ctypes.byref(need)) == _native.ERR_INVALID_ARGUMENT
+    assert b"bits" in lib.kvssd_b200_last_error()  # restype c_char_p: the text, not an int
+    assert callable(scope["fused_decode"])
