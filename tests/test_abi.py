@@ -127,3 +127,36 @@ def test_documented_ctypes_stub_binds():
                                                 ctypes.byref(need)) == _native.ERR_INVALID_ARGUMENT
     assert b"bits" in lib.kvssd_b200_last_error()  # restype c_char_p: the text, not an int
     assert callable(scope["fused_decode"])
+
+
+C_HOST = r"""
+#include <stdio.h>
+#include <string.h>
+#include "kvssd_b200.h"
+
+int main(void) {
+  size_t bytes = 0;
+  /* bits = 3 is refused before the query reaches the device */
+  int st = kvssd_b200_decode_workspace_size(1, 8, 4, 2, 32, 3, 16, &bytes);
+  if (st != KVSSD_B200_ERR_INVALID_ARGUMENT) return 1;
+  if (!strstr(kvssd_b200_last_error(), "bits")) return 2;
+  printf("%d|%s\n", kvssd_b200_version(), kvssd_b200_status_string(st));
+  return 0;
+}
+"""
+
+
+def test_plain_c_host_builds_and_links(tmp_path):
+    """A C99 host (the language a cgo or JNI shim is written in) compiles against the header
+    with -pedantic -Werror, links libkvssd_b200.so and calls its host-side entry points."""
+    src = tmp_path / "host.c"
+    src.write_text(C_HOST)
+    exe = tmp_path / "host"
+    lib_dir = _native.LIB_PATH.parent
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror",
+                    "-I", str(ROOT / "include"), str(src), "-o", str(exe), f"-L{lib_dir}",
+                    "-lkvssd_b200", f"-Wl,-rpath,{lib_dir}"], check=True)
+    done = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert done.returncode == 0, done.stderr
+    version, text = done.stdout.strip().split("|", 1)
+    assert int(version) == _native.library().kvssd_b200_version() and text
