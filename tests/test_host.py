@@ -259,3 +259,76 @@ def test_native_record_reader_matches_pread(tmp_path: Path):
     store2 = KVCacheStore.open(tmp_path / "s")
     with pytest.raises(OSError, match="short read"):
         store2.read_records(0, [store.blocks_for_layer(0)[-1]])
+
+
+PREAD_SHIM = r"""
+#define _GNU_SOURCE
+#include <dlfcn.h>
+#include <errno.h>
+#include <fcntl.h>
+#include <sys/types.h>
+
+/* pread that refuses every read of a descriptor opened with O_DIRECT, as a file system that
+   accepts the O_DIRECT open but not its reads does */
+static ssize_t refuse(int fd, void* buf, size_t n, off_t off, const char* name) {
+  typedef ssize_t (*fn)(int, void*, size_t, off_t);
+  fn real = (fn)dlsym(RTLD_NEXT, name);
+  int fl = fcntl(fd, F_GETFL);
+  if (fl >= 0 && (fl & O_DIRECT)) { errno = EINVAL; return -1; }
+  return real(fd, buf, n, off);
+}
+ssize_t pread(int fd, void* buf, size_t n, off_t off) { return refuse(fd, buf, n, off, "pread"); }
+ssize_t pread64(int fd, void* buf, size_t n, off_t off) {
+  return refuse(fd, buf, n, off, "pread64");
+}
+"""
+
+READER_CHILD = r"""
+import ctypes, mmap, sys
+from kvssd_b200 import _native
+path, n = sys.argv[1], 6
+lib = _native.library()
+buf = mmap.mmap(-1, n * 4096)  # page aligned, as O_DIRECT wants
+addr = ctypes.addressof(ctypes.c_char.from_buffer(buf))
+offsets = (ctypes.c_longlong * n)(*[4096 * (n - 1 - i) for i in range(n)])  # reversed
+used = ctypes.c_int(-1)
+st = lib.kvssd_b200_read_records(path.encode(), offsets, n, 4096, addr, 3, 1, ctypes.byref(used))
+ok = st == 0 and all(buf[i * 4096:(i + 1) * 4096] == bytes([n - 1 - i]) * 4096 for i in range(n))
+print(st, used.value, int(ok), lib.kvssd_b200_io_last_error().decode())
+"""
+
+
+def test_native_reader_falls_back_when_direct_reads_are_refused(tmp_path: Path):
+    """Where the O_DIRECT open succeeds but its reads fail with EINVAL, the native reader reads
+    the batch again with buffered preads (the store's default backend is ``buffered``, which
+    must not fail where kvssd's positioned reads succeed). The refusal comes from a preloaded
+    fake of pread in a child process."""
+    import os
+    import subprocess
+    import sys
+
+    data = tmp_path / "records.bin"
+    data.write_bytes(b"".join(bytes([i]) * 4096 for i in range(6)))
+    try:
+        os.close(os.open(data, os.O_RDONLY | os.O_DIRECT))
+    except OSError:
+        pytest.skip("this file system refuses O_DIRECT opens; the fallback is not reached")
+    shim_src = tmp_path / "shim.c"
+    shim_src.write_text(PREAD_SHIM)
+    shim = tmp_path / "shim.so"
+    subprocess.run(["gcc", "-shared", "-fPIC", "-O1", str(shim_src), "-o", str(shim), "-ldl"],
+                   check=True)
+    package = str(Path(__file__).resolve().parents[1] / "kvssd-attention_b200")
+    env = {**os.environ, "PYTHONPATH": package + os.pathsep + os.environ.get("PYTHONPATH", "")}
+
+    def child(preload: bool) -> list[str]:
+        run_env = {**env, "LD_PRELOAD": str(shim)} if preload else env
+        done = subprocess.run([sys.executable, "-c", READER_CHILD, str(data)], env=run_env,
+                              capture_output=True, text=True, timeout=120)
+        assert done.returncode == 0, done.stderr
+        return done.stdout.strip().split(" ", 3)
+
+    st, used, ok, *_ = child(preload=False)
+    assert (st, used, ok) == ("0", "1", "1")  # O_DIRECT reads where the file system allows
+    st, used, ok, *_ = child(preload=True)
+    assert (st, used, ok) == ("0", "0", "1")  # refused, then read buffered
