@@ -57,8 +57,9 @@ int kvssd_b200_copy_records_h2d(const void* host_base, size_t host_bytes,
   g_map_error.clear();
   if (!host_base || !offsets || !device_destination || n_records < 0 || record_bytes == 0)
     return map_fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "bad arguments");
-  for (int i = 0; i < n_records; ++i)
-    if (offsets[i] < 0 || static_cast<unsigned long long>(offsets[i]) + record_bytes > host_bytes)
+  for (int i = 0; i < n_records; ++i)  // offset + record_bytes <= host_bytes, without overflow
+    if (offsets[i] < 0 || record_bytes > host_bytes ||
+        static_cast<unsigned long long>(offsets[i]) > host_bytes - record_bytes)
       return map_fail(KVSSD_B200_ERR_INVALID_ARGUMENT,
                       "record " + std::to_string(i) + " lies outside the mapped range");
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

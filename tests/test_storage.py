@@ -77,6 +77,11 @@ def test_mapped_backend_and_record_copy_refusals_without_a_gpu(tmp_path):
                                          ctypes.addressof(host), None)
     assert st == _native.ERR_INVALID_ARGUMENT
     assert "outside the mapped range" in lib.kvssd_b200_host_last_error().decode()
+    wrap = (ctypes.c_longlong * 1)(4096)  # offset + record_bytes wraps around 2^64
+    st = lib.kvssd_b200_copy_records_h2d(ctypes.addressof(host), 8192, wrap, 1, 2**64 - 4096,
+                                         ctypes.addressof(host), None)
+    assert st == _native.ERR_INVALID_ARGUMENT
+    assert "outside the mapped range" in lib.kvssd_b200_host_last_error().decode()
     assert lib.kvssd_b200_host_register(None, 0, 1) == _native.ERR_INVALID_ARGUMENT
     store.close()
 
