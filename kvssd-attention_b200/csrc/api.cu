@@ -113,7 +113,7 @@ int check_geometry(const Geometry& g) {
   if (g.bt < 1 || g.qh < 1 || g.kvh < 1 || g.d < 1 || g.group < 1)
     return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "all dimensions must be positive");
   if (g.d % g.group) return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "group_size must divide head_dim");
-  if ((g.d * g.bits) % 8)
+  if ((static_cast<long long>(g.d) * g.bits) % 8)  // wide: head_dim is not yet bounded here
     return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "packed dimension does not match query head dimension");
   if (g.group % (8 / g.bits))
     return fail(KVSSD_B200_ERR_INVALID_ARGUMENT, "group_size must be positive and pack-aligned");

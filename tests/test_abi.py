@@ -62,6 +62,7 @@ def test_workspace_query_rejects_bad_geometry_before_touching_cuda():
         ((1, 8, 4, 2, 32, 4, 12), b"divide"),
         ((1, 8, 3, 2, 32, 4, 16), b"divisible by KV heads"),
         ((1, 8, 4, 2, 36, 2, 6), b"pack-aligned"),
+        ((1, 8, 4, 2, 2**31 - 1, 4, 1), b"packed dimension"),  # checked before head_dim <= 256
     ]
     for geom, msg in cases:
         assert lib.kvssd_b200_decode_workspace_size(*geom, ctypes.byref(n)) == _native.ERR_INVALID_ARGUMENT
