@@ -191,25 +191,60 @@ class ShardedDecoder:
         self._peer: PeerExchange | None = None
         self._peer_out: tuple[torch.Tensor, torch.Tensor] | None = None
         self._device: torch.device | None = None  # the device of the last run
+        self._stand_in: tuple | None = None  # (shape key, one-block empty batch) for empty shards
 
     def _use_peer(self, query: torch.Tensor, local: PackedBatch) -> bool:
         """Token shards on CUDA with a native streaming kernel (INT4 or INT2, head_dim 128, group
-        32/64, 16-byte aligned operands) and more than one rank: one fused kernel per rank."""
+        32/64) and more than one rank: one fused kernel per rank.
+
+        Decided from what every rank shares -- the geometry, not the number of blocks, their
+        alignment or whether this rank holds any -- so that all ranks take the same transport:
+        a rank that chose the all-gather while the others ran the exchange kernel would leave
+        both sides waiting for a partner. The kernel choice depends on the geometry alone."""
         if self.transport == "nccl" or self.mode != "tokens" or self.decode_fn is not None:
             return False
-        if self.world == 1 or query.device.type != "cuda" or local.packed_k.shape[0] == 0:
+        if self.world == 1 or query.device.type != "cuda":
             return False
         from . import ops
 
-        plan = ops.decode_plan(local.packed_k.shape[0], local.packed_k.shape[1], query.shape[0],
-                               local.packed_k.shape[2], query.shape[1], local.bits,
-                               local.group_size)
-        aligned = all(t.data_ptr() % 16 == 0 for t in (local.packed_k, local.packed_v,
-                                                        local.scales_k, local.scales_v))
-        ok = plan["kernel"] in ops.STREAMING_KERNELS and aligned
+        _, block_tokens, kv_heads, _ = local.packed_k.shape
+        plan = ops.decode_plan(1, block_tokens, query.shape[0], kv_heads, query.shape[1],
+                               local.bits, local.group_size)
+        ok = plan["kernel"] in ops.STREAMING_KERNELS
         if self.transport == "peer" and not ok:
-            raise RuntimeError("peer transport needs the streaming kernel's shapes and alignment")
+            raise RuntimeError("peer transport needs the streaming kernel's shapes")
         return ok
+
+    def _peer_operands(self, local: PackedBatch) -> PackedBatch:
+        """The shard as the exchange kernel takes it. An empty shard joins the exchange as a
+        one-block stand-in with no valid tokens, for which the kernel returns out 0 and lse -inf
+        (no weight in the ranks' merge); operands that are not contiguous and 16-byte aligned
+        are copied. The stand-in is kept for later calls of the same shape."""
+        if local.packed_k.shape[0] == 0:
+            _, block_tokens, kv_heads, packed_dim = local.packed_k.shape
+            groups = local.scales_k.shape[3]
+            key = (block_tokens, kv_heads, packed_dim, groups, local.scales_k.dtype,
+                   local.packed_k.device, local.bits, local.group_size)
+            if self._stand_in is None or self._stand_in[0] != key:
+                dev = local.packed_k.device
+                codes = torch.zeros((1, block_tokens, kv_heads, packed_dim), dtype=torch.uint8,
+                                    device=dev)
+                scales = torch.zeros((1, block_tokens, kv_heads, groups),
+                                     dtype=local.scales_k.dtype, device=dev)
+                self._stand_in = (key, replace(local, packed_k=codes, packed_v=codes,
+                                               scales_k=scales, scales_v=scales,
+                                               valid_tokens=torch.zeros(1, dtype=torch.int32,
+                                                                        device=dev)))
+            return self._stand_in[1]
+
+        def ready(t: torch.Tensor) -> torch.Tensor:
+            if t.is_contiguous() and t.data_ptr() % 16 == 0:
+                return t
+            return t.clone(memory_format=torch.contiguous_format)
+
+        return replace(local, packed_k=ready(local.packed_k), packed_v=ready(local.packed_v),
+                       scales_k=ready(local.scales_k), scales_v=ready(local.scales_v),
+                       valid_tokens=local.valid_tokens.to(torch.int32).contiguous())
 
     def check(self) -> None:
         """Collective failure check: every rank of the group calls it at the same point.
@@ -339,8 +374,9 @@ class ShardedDecoder:
             self._peer_out = (torch.empty((qh, d), dtype=torch.float32, device=query.device),
                               torch.empty((qh,), dtype=torch.float32, device=query.device))
         PackedBatch.validate(local, query)
+        local = self._peer_operands(local)
         out, lse = self._peer_out
         return ops.decode_exchange(
             query, local.packed_k, local.packed_v, local.scales_k, local.scales_v,
-            local.valid_tokens.to(torch.int32).contiguous(), local.bits, local.group_size,
+            local.valid_tokens, local.bits, local.group_size,
             sm_scale, self._peer.rank, self._peer.world, self._peer.buffers, out=out, lse=lse)

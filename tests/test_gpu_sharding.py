@@ -4,9 +4,10 @@ reference backend's frozen output for the whole context -- token shards through 
 peer-memory exchange kernel and through NCCL, and KV-head shards -- and the c2 configuration
 (1024 blocks) split over 2, 4 and 8 ranks through the peer exchange against its frozen output.
 Every call on every rank must give the same bits. Also: the peer exchange under CUDA-graph
-replay, and a rank that skips a call (the other rank's kernel gives up after about a second,
-flags status bit 8 and returns NaN; the group's collective check raises on every rank and
-re-arms the buffers; nothing faults or hangs; NVLS is off)."""
+replay, ranks whose shards are empty or unaligned (they take the exchange like the others),
+and a rank that skips a call (the other rank's kernel gives up after about a second, flags
+status bit 8 and returns NaN; the group's collective check raises on every rank and re-arms
+the buffers; nothing faults or hangs; NVLS is off)."""
 
 from __future__ import annotations
 
@@ -152,6 +153,49 @@ def test_peer_exchange_replays_in_cuda_graph():
     for rank in (0, 1):
         same, status = results[rank]
         assert same and status == 0
+
+
+def _uneven_main(rank: int, world: int, port: int, results) -> None:
+    """One selected block over the ranks: every rank but 0 holds an empty shard, and rank 0's
+    codes are a view 8 bytes off 16-byte alignment. Every rank still takes the peer exchange
+    (the choice rests on the shared geometry), and the result is rank 0's block alone."""
+    device, w, batch, q = _setup(rank, world, port)
+    try:
+        from dataclasses import replace
+
+        from kvssd_b200 import ops
+        from kvssd_b200.sharding import ShardedDecoder, shard_batch_by_blocks
+
+        scale = 1.0 / math.sqrt(w.head_dim)
+        one = replace(batch, packed_k=batch.packed_k[:1], packed_v=batch.packed_v[:1],
+                      scales_k=batch.scales_k[:1], scales_v=batch.scales_v[:1],
+                      valid_tokens=batch.valid_tokens[:1])
+        local = shard_batch_by_blocks(one, rank, world)
+        if rank == 0:
+            raw = torch.empty(local.packed_k.numel() + 8, dtype=torch.uint8, device=device)
+            view = raw[8:].view(local.packed_k.shape)
+            view.copy_(local.packed_k)
+            local = replace(local, packed_k=view)
+        dec = ShardedDecoder("tokens")
+        runs = [tuple(t.clone() for t in dec.run(q, local, scale)) for _ in range(2)]
+        ref_out, ref_lse = ops.decode(q, *(t.contiguous() for t in (
+            one.packed_k, one.packed_v, one.scales_k, one.scales_v)),
+            one.valid_tokens.to(torch.int32).contiguous(), w.bits, w.group_size, scale)
+        torch.cuda.synchronize(device)
+        close = all(torch.allclose(o, ref_out, atol=1e-5, rtol=1e-5) and
+                    torch.allclose(lse, ref_lse, atol=1e-5, rtol=1e-5) for o, lse in runs)
+        results[rank] = (close, dec._peer is not None, ops.read_device_status_all(device))
+        dec.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [pytest.param(n, marks=_needs(n)) for n in (2, 4)])
+def test_peer_exchange_with_empty_and_unaligned_shards(world):
+    results = _spawn(_uneven_main, world=world)
+    for rank in range(world):
+        close, used_peer, status = results[rank]
+        assert used_peer and status == 0 and close
 
 
 def _skip_main(rank: int, world: int, port: int, results) -> None:

@@ -130,3 +130,79 @@ def test_sharded_decode_matches_whole_batch(world, mode):
         out, lse, _ = results[rank]
         np.testing.assert_allclose(out, g["out"], atol=2e-5, rtol=1e-5)
         np.testing.assert_allclose(lse, g["lse"], atol=2e-5, rtol=1e-6)
+
+
+def test_peer_transport_choice_ignores_the_local_shard(monkeypatch):
+    """Every rank of a token-sharded group takes the same transport: the choice rests on the
+    geometry the ranks share, never on this rank's block count, alignment or emptiness (a rank
+    that took the all-gather while the others ran the exchange kernel would leave both waiting).
+    The planner is stubbed and the query is a CUDA-typed stand-in; nothing runs on a device."""
+    from types import SimpleNamespace
+
+    from kvssd_b200 import ops
+    from kvssd_b200.sharding import ShardedDecoder
+
+    g = load_npz(GOLDEN)
+    _, batch = _batch(g)
+    calls = []
+
+    def plan(*args):
+        calls.append(args)
+        return {"kernel": "tensor_core_tma"}
+
+    monkeypatch.setattr(ops, "decode_plan", plan)
+    monkeypatch.setattr(ShardedDecoder, "world", property(lambda self: 2))
+    query = SimpleNamespace(device=torch.device("cuda", 0), shape=(32, 128))
+    raw = torch.empty(batch.packed_k.numel() + 8, dtype=torch.uint8)
+    misaligned = raw[8:].view(batch.packed_k.shape)
+    n = batch.packed_k.shape[0]
+    shards = [batch, shard_batch_by_blocks(batch, 2 * n - 1, 2 * n),  # the last rank's: empty
+              PackedBatch(misaligned, *(getattr(batch, f) for f in
+                                        ("packed_v", "scales_k", "scales_v", "valid_tokens",
+                                         "bits", "group_size")))]
+    assert shards[1].packed_k.shape[0] == 0
+    for transport in ("auto", "peer"):
+        dec = ShardedDecoder("tokens", transport=transport)
+        assert [dec._use_peer(query, s) for s in shards] == [True] * 3
+    assert len(set(calls)) == 1  # the same question on every rank, whatever its shard holds
+    monkeypatch.setattr(ops, "decode_plan", lambda *a: {"kernel": "tensor_core_regs"})
+    assert not ShardedDecoder("tokens")._use_peer(query, shards[1])
+    with pytest.raises(RuntimeError, match="peer transport"):
+        ShardedDecoder("tokens", transport="peer")._use_peer(query, shards[0])
+
+
+def test_peer_operands_stand_in_for_empty_and_unaligned_shards():
+    """What the exchange kernel is given: an empty shard becomes one block with no valid tokens
+    (the kernel returns out 0 and lse -inf for it, no weight in the merge), kept for later calls;
+    operands that are not 16-byte aligned or not contiguous are copied; the rest pass as they
+    are."""
+    from kvssd_b200.sharding import ShardedDecoder
+
+    g = load_npz(GOLDEN)
+    _, batch = _batch(g)
+    dec = ShardedDecoder("tokens")
+    n = batch.packed_k.shape[0]
+    empty = shard_batch_by_blocks(batch, 2 * n - 1, 2 * n)  # the last rank's shard: no blocks
+    stand_in = dec._peer_operands(empty)
+    _, bt, kvh, pd = batch.packed_k.shape
+    assert stand_in.packed_k.shape == (1, bt, kvh, pd) and stand_in.packed_v.shape == (1, bt, kvh, pd)
+    assert stand_in.scales_k.shape == (1, bt, kvh, batch.scales_k.shape[3])
+    assert stand_in.scales_k.dtype == batch.scales_k.dtype
+    assert stand_in.valid_tokens.tolist() == [0] and stand_in.valid_tokens.dtype == torch.int32
+    assert (stand_in.bits, stand_in.group_size) == (batch.bits, batch.group_size)
+    assert dec._peer_operands(empty) is stand_in  # reused, not reallocated per call
+
+    same = dec._peer_operands(batch)
+    for f in ("packed_k", "packed_v", "scales_k", "scales_v"):
+        assert getattr(same, f) is getattr(batch, f)
+    raw = torch.empty(batch.packed_k.numel() + 8, dtype=torch.uint8)
+    misaligned = raw[8:].view(batch.packed_k.shape)
+    misaligned.copy_(batch.packed_k)
+    strided = batch.scales_v.transpose(1, 2).contiguous().transpose(1, 2)
+    fixed = dec._peer_operands(PackedBatch(misaligned, batch.packed_v, batch.scales_k, strided,
+                                           batch.valid_tokens.long(), batch.bits,
+                                           batch.group_size))
+    assert fixed.packed_k.data_ptr() % 16 == 0 and torch.equal(fixed.packed_k, batch.packed_k)
+    assert fixed.scales_v.is_contiguous() and torch.equal(fixed.scales_v, batch.scales_v)
+    assert fixed.packed_v is batch.packed_v
+    assert fixed.valid_tokens.dtype == torch.int32
