@@ -47,9 +47,11 @@ class B200AttentionBackend:
 
         Kernel failures surface the way the reference's TORCH_CHECK does, as an exception,
         but without a host synchronisation per call: the call's device status word is copied
-        into pinned memory after its kernels, and the next ``run`` on the same stream (or
-        ``check``) raises ops.DeviceFailure (a RuntimeError) if that word flagged a failure.
-        The failed call's own out/lse are NaN, so nothing plausible is returned meanwhile.
+        into pinned memory after its kernels, and a later ``run`` on the same stream raises
+        ops.DeviceFailure (a RuntimeError) if that word flagged a failure -- the first one
+        after the copy has landed, and at the latest the fourth, which waits for it -- as does
+        ``check``, which waits. The failed call's own out/lse are NaN, and so are those of every
+        call after it until the word is cleared, so nothing plausible is returned meanwhile.
         """
         PackedBatch.validate(batch, query)
         if query.device.type != "cuda":

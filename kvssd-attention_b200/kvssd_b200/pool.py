@@ -127,9 +127,10 @@ class DeviceBlockPool:
                      lse: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
         """(out fp32, lse fp32) over the pool slots in ``table`` (None = every slot).
 
-        Asynchronous; a kernel failure (a table entry outside the pool, a wait that gave up)
-        makes that call's result NaN and raises ops.DeviceFailure on the next decode on this
-        stream or on ``check()``."""
+        Asynchronous; a kernel failure (a table entry outside the pool is skipped and flagged;
+        after a wait that gave up the call's result is NaN) raises ops.DeviceFailure on a later
+        decode on this stream once the status read has landed (at the latest four calls on),
+        or on ``check()``, which waits for it."""
         scale = sm_scale if sm_scale is not None else 1.0 / math.sqrt(query.shape[-1])
         watch = ops.status_watch(self.device)
         watch.poll("DeviceBlockPool.decode (an earlier call)")
