@@ -17,6 +17,7 @@ from pathlib import Path
 
 import torch
 
+from ._registry import FactoryTable
 from .format import BlockEntry
 
 ALIGNMENT = 4096
@@ -381,15 +382,20 @@ class MappedStorageBackend:
                 self._registered = 0
 
 
-_FACTORIES = {"gds": GDSStorageBackend, "direct": DirectStorageBackend,
-              "buffered": BufferedStorageBackend, "mapped": MappedStorageBackend}
+# kvssd's three backends, in the order ``auto`` tries them, then ``mapped``, which ``auto``
+# never picks (it pins the whole file in host memory)
+_table = FactoryTable("storage")
+for _name, _factory in (("gds", GDSStorageBackend), ("direct", DirectStorageBackend),
+                        ("buffered", BufferedStorageBackend)):
+    _table.add(_name, _factory, auto=True)
+_table.add("mapped", MappedStorageBackend, auto=False)
 
 
 def register_storage_backend(name: str, factory) -> None:
-    key = name.strip().lower()
-    if key in ("", "auto"):
-        raise ValueError("backend name must be non-empty and cannot be 'auto'")
-    _FACTORIES[key] = factory
+    """Adds (or replaces) a backend under ``name`` (case-insensitive, not 'auto'). As in
+    kvssd, ``auto`` only considers the names gds, direct and buffered, so a factory registered
+    under one of those replaces that step of ``auto``; other names are chosen explicitly."""
+    _table.add(name, factory)
 
 
 def _close(backend) -> None:
@@ -402,8 +408,8 @@ def available_storage_backends(path: str | Path) -> list[StorageAvailability]:
     """The probe result of every registered backend for ``path``; each probed instance is closed
     again (a gds probe opens a cuFile handle and an O_DIRECT descriptor)."""
     states = []
-    for factory in _FACTORIES.values():
-        backend = factory(Path(path))
+    for key in _table.names():
+        backend = _table.factory(key)(Path(path))
         try:
             states.append(backend.probe())
         finally:
@@ -414,26 +420,7 @@ def available_storage_backends(path: str | Path) -> list[StorageAvailability]:
 def resolve_storage_backend(requested, path: str | Path):
     """An instance (probed), a registered name, or ``auto``/None: gds, direct, buffered in that
     order of preference. Unavailable explicit choices raise RuntimeError; unknown names
-    ValueError (kvssd's messages)."""
+    ValueError (kvssd's messages). Probed instances that are not returned are closed."""
     path = Path(path)
-    if requested is not None and not isinstance(requested, str):
-        state = requested.probe()
-        if not state.available:
-            raise RuntimeError(f"storage backend '{state.name}' unavailable: {state.reason}")
-        return requested
-    key = (requested or "auto").strip().lower()
-    if key == "auto":
-        for name in ("gds", "direct", "buffered"):  # not "mapped": it pins the whole file
-            backend = _FACTORIES[name](path)
-            if backend.probe().available:
-                return backend
-            _close(backend)
-        raise RuntimeError(f"no storage backend is available for {path}")
-    if key not in _FACTORIES:
-        listed = ", ".join(["auto", *_FACTORIES])
-        raise ValueError(f"unknown storage backend '{key}'; choose one of: {listed}")
-    backend = _FACTORIES[key](path)
-    state = backend.probe()
-    if not state.available:
-        raise RuntimeError(f"storage backend '{key}' unavailable: {state.reason}")
-    return backend
+    return _table.resolve(requested, lambda factory: factory(path),
+                          lambda backend: backend.probe(), path, release=_close)

@@ -332,3 +332,31 @@ def test_native_reader_falls_back_when_direct_reads_are_refused(tmp_path: Path):
     assert (st, used, ok) == ("0", "1", "1")  # O_DIRECT reads where the file system allows
     st, used, ok, *_ = child(preload=True)
     assert (st, used, ok) == ("0", "0", "1")  # refused, then read buffered
+
+
+def test_registered_attention_backend_takes_part_in_auto(monkeypatch):
+    """Every registered attention backend is open to ``auto``, in registration order after the
+    ``cuda`` kernels: on a CPU device a CPU backend the caller registered is the one chosen."""
+    from kvssd_b200.backends import BackendAvailability, registry
+
+    table = registry.FactoryTable("attention")
+    for name, (factory, auto) in registry._table._entries.items():
+        table.add(name, factory, auto=auto)
+    monkeypatch.setattr(registry, "_table", table)
+
+    class CpuOnly:
+        name = "cpu-only"
+
+        def probe(self, device):
+            ok = torch.device(device).type == "cpu"
+            return BackendAvailability(self.name, ok, False, False, "test double",
+                                       torch.device(device).type)
+
+        def run(self, query, batch, sm_scale):
+            raise AssertionError
+
+    register_attention_backend("cpu-only", CpuOnly)
+    assert isinstance(resolve_attention_backend("auto", "cpu"), CpuOnly)
+    assert [a.name for a in available_attention_backends("cpu")] == ["cuda", "cpu-only"]
+    with pytest.raises(ValueError, match="choose one of: auto, cuda, cpu-only"):
+        resolve_attention_backend("triton", "cpu")

@@ -106,8 +106,10 @@ def test_backend_probes_are_closed_again(tmp_path, monkeypatch):
 
     store = _store(tmp_path)
     path = store.root / "blocks.kvssd"
-    factories = {"gds": Unavailable, "direct": Counting, "buffered": Counting}
-    monkeypatch.setattr(storage, "_FACTORIES", factories)
+    table = storage.FactoryTable("storage")
+    for name, factory in (("gds", Unavailable), ("direct", Counting), ("buffered", Counting)):
+        table.add(name, factory, auto=True)
+    monkeypatch.setattr(storage, "_table", table)
     states = available_storage_backends(path)
     assert [s.available for s in states] == [False, True, True]
     assert closed == ["gds", "buffered", "buffered"]  # Counting's name is "buffered"
@@ -115,4 +117,51 @@ def test_backend_probes_are_closed_again(tmp_path, monkeypatch):
     chosen = resolve_storage_backend("auto", path)
     assert closed == ["gds"] and chosen.probe().available  # the chosen one stays open
     chosen.close()
+    store.close()
+
+
+def test_registered_storage_backends_and_auto(tmp_path, monkeypatch):
+    """As in kvssd, ``auto`` considers only gds, direct and buffered: a factory registered under
+    one of those names replaces that step, one under a new name is chosen only by name. A
+    backend that is built, found unavailable and not returned is closed."""
+    from kvssd_b200 import register_storage_backend, storage
+
+    table = storage.FactoryTable("storage")
+    for name, factory in storage._table._entries.items():
+        table.add(name, factory[0], auto=factory[1])
+    monkeypatch.setattr(storage, "_table", table)
+    store = _store(tmp_path)
+    path = store.root / "blocks.kvssd"
+    closed = []
+
+    class Mine(BufferedStorageBackend):
+        name = "mine"
+
+        def close(self) -> None:
+            closed.append(self.name)
+            super().close()
+
+    class Refused(Mine):
+        name = "refused"
+
+        def probe(self):
+            return storage.StorageAvailability(self.name, False, False, False, "not today")
+
+    register_storage_backend(" Mine ", Mine)
+    assert resolve_storage_backend("auto", path).name in ("gds", "direct", "buffered")
+    assert isinstance(resolve_storage_backend("MINE", path), Mine)
+    register_storage_backend("refused", Refused)
+    with pytest.raises(RuntimeError, match="storage backend 'refused' unavailable: not today"):
+        resolve_storage_backend("refused", path)
+    assert closed == ["refused"]
+    for name in ("gds", "direct"):
+        register_storage_backend(name, Refused)  # both steps of auto now refuse
+    register_storage_backend("buffered", Mine)
+    assert isinstance(resolve_storage_backend(None, path), Mine)
+    assert closed == ["refused", "refused", "refused"]
+    assert table.names()[:4] == ["gds", "direct", "buffered", "mapped"]  # places kept
+    with pytest.raises(ValueError, match="cannot be 'auto'"):
+        register_storage_backend("Auto", Mine)
+    with pytest.raises(ValueError, match="choose one of: auto, gds, direct, buffered, mapped, mine"):
+        resolve_storage_backend("nvme", path)
     store.close()
