@@ -72,7 +72,9 @@ KVSSD_B200_API int kvssd_b200_version(void);
 /* Static description of a status code. No reference counterpart. */
 KVSSD_B200_API const char* kvssd_b200_status_string(int status);
 
-/* Detail of the last error raised on the calling thread (empty if none). */
+/* Detail of the last error raised on the calling thread (empty if none). No reference
+ * counterpart: the reference op raises the message through TORCH_CHECK
+ * (csrc/bindings.cpp:26-38). */
 KVSSD_B200_API const char* kvssd_b200_last_error(void);
 
 /* Bytes of device workspace kvssd_b200_decode needs for this geometry on the current device.
@@ -201,6 +203,26 @@ KVSSD_B200_API int kvssd_b200_read_records(const char* path, const long long* of
                                            int threads, int direct, int* used_direct);
 KVSSD_B200_API const char* kvssd_b200_io_last_error(void);
 
+/* Page-locked store files (the "mapped" storage backend): host_register registers a host
+ * range -- a store file mapped read-only with mmap, read_only = 1 -- with the CUDA driver
+ * (cudaHostRegister, portable; read-only where asked), and copy_records_h2d then copies
+ * n_records records of record_bytes at byte offsets of that range into device_destination +
+ * i * record_bytes on `stream`, asynchronously, one cudaMemcpyAsync per run of records that are
+ * consecutive in the file: the records travel by DMA from the page cache, with no reader
+ * threads and no staging copy (the reference reads them into a host buffer first,
+ * src/kvssd/storage/buffered.py:53-76, src/kvssd/pipeline.py:118-165). A record that does not
+ * lie wholly inside [0, host_bytes) is refused (KVSSD_B200_ERR_INVALID_ARGUMENT) before anything
+ * is copied;
+ * a range the driver will not register gives KVSSD_B200_ERR_UNSUPPORTED with the reason in
+ * kvssd_b200_host_last_error. */
+KVSSD_B200_API int kvssd_b200_host_register(void* ptr, size_t bytes, int read_only);
+KVSSD_B200_API int kvssd_b200_host_unregister(void* ptr);
+KVSSD_B200_API int kvssd_b200_copy_records_h2d(const void* host_base, size_t host_bytes,
+                                               const long long* offsets, int n_records,
+                                               size_t record_bytes, void* device_destination,
+                                               kvssd_b200_stream_t stream);
+KVSSD_B200_API const char* kvssd_b200_host_last_error(void);
+
 /* GPUDirect Storage (cuFile) reads of whole records straight into device memory: kvssd's
  * "gds" storage backend (src/kvssd/storage/gds.py:13-94 over csrc/gds_bindings.cpp:21-98,
  * GDSFile: cuFileDriverOpen, O_DIRECT open, cuFileHandleRegister, cuFileRead). libcufile is
@@ -212,25 +234,6 @@ KVSSD_B200_API const char* kvssd_b200_io_last_error(void);
  * `threads` reader threads; synchronous (the data is in device memory on return). Errors:
  * KVSSD_B200_ERR_INVALID_ARGUMENT for misaligned requests, KVSSD_B200_ERR_CUDA for a failed or
  * short cuFileRead (the reference raises OSError / EOFError). */
-/* Page-locked store files (the "mapped" storage backend): host_register registers a host
- * range -- a store file mapped read-only with mmap, read_only = 1 -- with the CUDA driver
- * (cudaHostRegister, portable; read-only where asked), and copy_records_h2d then copies
- * n_records records of record_bytes at byte offsets of that range into device_destination +
- * i * record_bytes on `stream`, asynchronously, one cudaMemcpyAsync per run of records that are
- * consecutive in the file: the records travel by DMA from the page cache, with no reader
- * threads and no staging copy (the reference reads them into a host buffer first,
- * src/kvssd/storage/buffered.py:53-76, src/kvssd/pipeline.py:118-165). Offsets outside
- * [0, host_bytes) are refused (KVSSD_B200_ERR_INVALID_ARGUMENT) before anything is copied;
- * a range the driver will not register gives KVSSD_B200_ERR_UNSUPPORTED with the reason in
- * kvssd_b200_host_last_error. */
-KVSSD_B200_API int kvssd_b200_host_register(void* ptr, size_t bytes, int read_only);
-KVSSD_B200_API int kvssd_b200_host_unregister(void* ptr);
-KVSSD_B200_API int kvssd_b200_copy_records_h2d(const void* host_base, size_t host_bytes,
-                                               const long long* offsets, int n_records,
-                                               size_t record_bytes, void* device_destination,
-                                               kvssd_b200_stream_t stream);
-KVSSD_B200_API const char* kvssd_b200_host_last_error(void);
-
 typedef struct kvssd_b200_gds_file kvssd_b200_gds_file;
 KVSSD_B200_API int kvssd_b200_gds_open(const char* path, kvssd_b200_gds_file** file);
 KVSSD_B200_API int kvssd_b200_gds_read_records(kvssd_b200_gds_file* file,
@@ -258,7 +261,8 @@ typedef struct kvssd_b200_problem {
   int n_sel_blocks;
 } kvssd_b200_problem;
 
-/* Workspace bytes of kvssd_b200_decode_batched for n_problems problems. */
+/* Workspace bytes of kvssd_b200_decode_batched for n_problems problems. No reference
+ * counterpart. */
 KVSSD_B200_API int kvssd_b200_decode_batched_workspace_size(int n_problems, int block_tokens,
                       int query_heads, int kv_heads, int head_dim, int bits, int group_size,
                       size_t* bytes);
@@ -286,13 +290,14 @@ KVSSD_B200_API int kvssd_b200_exchange_bytes(int world, int query_heads, int hea
 
 /* Allocates and zeroes an exchange buffer on the current device (cudaMalloc; 256-byte
  * aligned), re-zeroes it (synchronously, e.g. after an exchange timeout) and frees it. Call
- * outside any stream capture. */
+ * outside any stream capture. No reference counterpart (the reference runs on one device). */
 KVSSD_B200_API int kvssd_b200_exchange_alloc(size_t bytes, void** buffer);
 KVSSD_B200_API int kvssd_b200_exchange_clear(void* buffer, size_t bytes);
 KVSSD_B200_API int kvssd_b200_exchange_free(void* buffer);
 
 /* CUDA IPC export of an exchange buffer into a KVSSD_B200_IPC_HANDLE_BYTES handle, import of a
- * peer process's handle (peer access enabled lazily) and release of the import. */
+ * peer process's handle (peer access enabled lazily) and release of the import. No reference
+ * counterpart (the reference runs on one device). */
 KVSSD_B200_API int kvssd_b200_ipc_handle(void* buffer, void* handle);
 KVSSD_B200_API int kvssd_b200_ipc_open(const void* handle, void** buffer);
 KVSSD_B200_API int kvssd_b200_ipc_close(void* buffer);
