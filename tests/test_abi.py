@@ -161,3 +161,17 @@ def test_plain_c_host_builds_and_links(tmp_path):
     assert done.returncode == 0, done.stderr
     version, text = done.stdout.strip().split("|", 1)
     assert int(version) == _native.library().kvssd_b200_version() and text
+
+
+def test_every_declaration_states_its_reference_counterpart():
+    """Each entry point's comment (its own, or that of the group it is declared in) cites the
+    reference interface it replaces (file:line) or says it has none."""
+    text = HEADER.read_text()
+    comments = [(m.end(), m.group(0)) for m in re.finditer(r"/\*.*?\*/", text, re.S)]
+    missing = []
+    for m in re.finditer(r"KVSSD_B200_API\s+[\w\s\*]+?\b(kvssd_b200_\w+)\s*\(", text):
+        before = [c for end, c in comments if end <= m.start()]
+        comment = before[-1] if before else ""
+        if not (re.search(r"\.(py|cu|cpp|h):\d", comment) or "counterpart" in comment):
+            missing.append(m.group(1))
+    assert not missing, missing
