@@ -175,3 +175,17 @@ def test_every_declaration_states_its_reference_counterpart():
         if not (re.search(r"\.(py|cu|cpp|h):\d", comment) or "counterpart" in comment):
             missing.append(m.group(1))
     assert not missing, missing
+
+
+def test_integration_guide_lists_every_entry_point():
+    """The integration guide's table names every exported function (groups may abbreviate the
+    shared prefix, as in `kvssd_b200_ipc_handle` / `_open` / `_close`)."""
+    guide = (ROOT / "INTEGRATION.md").read_text()
+    missing = []
+    for name in sorted(declared_functions()):
+        if name in guide:
+            continue
+        stem, _, tail = name.rpartition("_")  # abbreviated: `<stem>_first` / `_<tail>`
+        if f"`{stem}_" not in guide or f"`_{tail}`" not in guide:
+            missing.append(name)
+    assert not missing, missing
