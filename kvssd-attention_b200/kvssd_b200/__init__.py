@@ -29,6 +29,7 @@ from .selectors import AllBlocks, RecentSinkBlocks
 from .storage import (
     GDSStorageBackend,
     StorageAvailability,
+    StorageBackend,
     available_storage_backends,
     register_storage_backend,
     resolve_storage_backend,
@@ -46,6 +47,7 @@ __all__ = [
     "PackedBatch",
     "RecentSinkBlocks",
     "StorageAvailability",
+    "StorageBackend",
     "available_storage_backends",
     "available_attention_backends",
     "dequantize_tensor",

@@ -14,6 +14,7 @@ import sys
 import threading
 from dataclasses import dataclass
 from pathlib import Path
+from typing import Protocol, runtime_checkable
 
 import torch
 
@@ -30,6 +31,24 @@ class StorageAvailability:
     direct: bool
     asynchronous: bool
     reason: str
+
+
+@runtime_checkable
+class StorageBackend(Protocol):
+    """What KVCacheStore asks of a storage backend, kvssd's interface
+    (src/kvssd/storage/base.py:21-39): a probe, aligned buffers, single-record reads and
+    close. The backends here also offer ``read_records`` for batches of records."""
+
+    name: str
+
+    def probe(self) -> StorageAvailability: ...
+
+    def allocate_buffer(self, size: int, *, pinned: bool = False,
+                        device: torch.device | None = None) -> torch.Tensor: ...
+
+    def read_into(self, entry: BlockEntry, destination: torch.Tensor) -> None: ...
+
+    def close(self) -> None: ...
 
 
 def _aligned(size: int, device: torch.device | str | None = None, pinned: bool = False):

@@ -165,3 +165,15 @@ def test_registered_storage_backends_and_auto(tmp_path, monkeypatch):
     with pytest.raises(ValueError, match="choose one of: auto, gds, direct, buffered, mapped, mine"):
         resolve_storage_backend("nvme", path)
     store.close()
+
+
+def test_builtin_backends_satisfy_the_storage_interface(tmp_path):
+    """Every registered backend has kvssd's StorageBackend interface
+    (src/kvssd/storage/base.py:21-39), and the package exports it under kvssd's name."""
+    from kvssd_b200 import StorageBackend, storage
+
+    path = tmp_path / "blocks.kvssd"
+    for key in storage._table.names():
+        backend = storage._table.factory(key)(path)
+        assert isinstance(backend, StorageBackend), key
+        backend.close()
