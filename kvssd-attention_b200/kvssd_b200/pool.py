@@ -76,8 +76,9 @@ class DeviceBlockPool:
     @classmethod
     def from_store(cls, store, layer: int, device: torch.device | str,
                    verify_crc: bool = True) -> "DeviceBlockPool":
-        """Loads every block of ``layer``: the raw records are read into one pinned buffer,
-        copied to the device in one transfer and decoded there (header checks and the payload
+        """Loads every block of ``layer``: the raw records are read into one pinned buffer by
+        the native reader (KVCacheStore.read_records), copied to the device in one transfer and
+        decoded there (header checks and the payload
         CRC-32 on the GPU, ops.decode_records). Raises like kvssd's decode_record on a bad
         record: ValueError for a bad header or layout, IOError for a CRC mismatch."""
         device = torch.device(device)
@@ -87,10 +88,7 @@ class DeviceBlockPool:
         ids = store.blocks_for_layer(layer)
         if not ids:
             raise ValueError(f"layer {layer} has no blocks")
-        raw = torch.empty((len(ids), spec.record_bytes), dtype=torch.uint8,
-                          pin_memory=torch.cuda.is_available())
-        for i, b in enumerate(ids):
-            store.read_into(store.entry(layer, b), raw[i])
+        raw = store.read_records(layer, ids)  # one batch of the native reader, pinned
         dev = raw.to(device, non_blocking=True)
         kp, vp, ks, vs, valid, status = ops.decode_records(
             dev, spec, layer, torch.tensor(ids, dtype=torch.int32))
